@@ -1,0 +1,346 @@
+// The C ABI of libca_b200.so: argument validation (restating the checks of
+// `_C.mojo:87-316`), launch planning and kernel launches on the caller's
+// stream. Declarations and the contract live in include/cpu_attention_b200.h.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdio>
+#include <mutex>
+#include <string>
+
+#include "decode.cuh"
+#include "flash.cuh"
+#include "store.cuh"
+
+namespace {
+
+thread_local std::string g_cuda_error;
+
+int cuda_fail(cudaError_t e, const char* what) {
+  g_cuda_error = std::string(what) + ": " + cudaGetErrorString(e);
+  return CA_ECUDA;
+}
+
+bool head_dim_ok(long long e) { return e == 32 || e == 64 || e == 128; }
+bool page_ok(long long page) { return page > 0 && page % 16 == 0; }
+size_t elem_size(int dtype) { return dtype == CA_DTYPE_BF16 ? 2 : 4; }
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+struct DeviceInfo {
+  int sms = 0;
+  int max_smem_optin = 0;
+};
+
+std::mutex g_mutex;
+DeviceInfo g_devices[64];
+
+int device_info(int device, DeviceInfo* out) {
+  if (device < 0 || device >= 64) return CA_ECUDA;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  DeviceInfo& d = g_devices[device];
+  if (d.sms == 0) {
+    cudaError_t e = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(SMs)");
+    e = cudaDeviceGetAttribute(&d.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(smem)");
+  }
+  *out = d;
+  return CA_OK;
+}
+
+int current_device(int* dev) {
+  cudaError_t e = cudaGetDevice(dev);
+  return e == cudaSuccess ? CA_OK : cuda_fail(e, "cudaGetDevice");
+}
+
+// ---- decode plan ---------------------------------------------------------
+struct DecodePlan {
+  int cp, stages, warps, stage_bytes, kslot_bytes, page_bytes, warp_bytes, smem_bytes, ctas;
+};
+
+constexpr int kDecodeStageTarget = 16384;  // bytes of K+V per stage
+constexpr int kDecodeRingTarget = 49152;   // bytes of ring per warp
+constexpr int kDecodeMaxWarps = 8;
+
+bool decode_plan(long long head_dim, long long page, int dtype, const DeviceInfo& dev, DecodePlan* pl) {
+  const long long page_bytes = page * head_dim * (long long)elem_size(dtype);
+  if (page > ca::kDecodeMaxChunkTokens) return false;
+  int cp = (int)std::max(1LL, std::min((long long)ca::kDecodeMaxChunkTokens / page,
+                                       (long long)kDecodeStageTarget / (2 * page_bytes)));
+  pl->cp = cp;
+  pl->page_bytes = (int)page_bytes;
+  pl->kslot_bytes = (int)page_bytes + ca::kKSlotPadBytes;
+  pl->stage_bytes = cp * (pl->kslot_bytes + (int)page_bytes);
+  const int extra = (int)(head_dim * 4 + ca::kDecodeMaxChunkTokens * 4);
+  const int budget = dev.max_smem_optin - 1024;
+  int stages = std::max(2, std::min(4, kDecodeRingTarget / pl->stage_bytes));
+  auto warp_bytes = [&](int s) {
+    int w = s * pl->stage_bytes + extra + s * ((int)sizeof(ca::ChunkHdr) + 8);
+    return (w + 127) / 128 * 128;
+  };
+  while (stages > 2 && warp_bytes(stages) > budget) --stages;
+  if (warp_bytes(stages) > budget) return false;
+  pl->stages = stages;
+  pl->warp_bytes = warp_bytes(stages);
+  pl->warps = std::max(1, std::min(kDecodeMaxWarps, budget / pl->warp_bytes));
+  pl->smem_bytes = pl->warps * pl->warp_bytes;
+  pl->ctas = dev.sms;
+  return true;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// workspace: [status int32 | pad to 256][partials: float, 2 slots per possible
+// worker warp, fixed per device][tickets: int32 per (sequence, head)]. The
+// tickets sit at a fixed offset so that no call's partials ever land on another
+// call's tickets, which must stay zero between calls.
+size_t decode_partial_bytes(const DeviceInfo& dev) {
+  return align256((size_t)2 * dev.sms * kDecodeMaxWarps * (128 + 2) * 4);
+}
+size_t decode_ws_bytes(long long batch, long long heads, const DeviceInfo& dev) {
+  return 256 + decode_partial_bytes(dev) + align256((size_t)(batch * heads) * 4);
+}
+
+template <typename T, int E>
+int launch_decode(const ca::DecodeParams& prm, const DecodePlan& pl, cudaStream_t stream, int device) {
+  static std::mutex mu;
+  static int configured[64] = {0};
+  auto kern = ca::decode_kernel<T, E>;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (configured[device] < pl.smem_bytes) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem_bytes);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(decode)");
+      configured[device] = pl.smem_bytes;
+    }
+  }
+  kern<<<pl.ctas, 32 * pl.warps, pl.smem_bytes, stream>>>(prm);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? CA_OK : cuda_fail(e, "decode launch");
+}
+
+template <typename T>
+int dispatch_decode(long long E, const ca::DecodeParams& prm, const DecodePlan& pl, cudaStream_t s, int dev) {
+  switch (E) {
+    case 32: return launch_decode<T, 32>(prm, pl, s, dev);
+    case 64: return launch_decode<T, 64>(prm, pl, s, dev);
+    default: return launch_decode<T, 128>(prm, pl, s, dev);
+  }
+}
+
+template <typename T, int E>
+int launch_store_e(const ca::StoreParams& prm, bool vec16, cudaStream_t stream) {
+  const int per_row = vec16 ? E / (16 / (int)sizeof(T)) : E;
+  const long long total = prm.tokens * prm.H * per_row;
+  if (total == 0) return CA_OK;
+  const int threads = 256;
+  const long long blocks = (total + threads - 1) / threads;
+  if (vec16)
+    ca::store_kernel<T, E, true><<<(unsigned)blocks, threads, 0, stream>>>(prm);
+  else
+    ca::store_kernel<T, E, false><<<(unsigned)blocks, threads, 0, stream>>>(prm);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? CA_OK : cuda_fail(e, "store launch");
+}
+
+int launch_store(const ca::StoreParams& prm, long long E, int dtype, bool vec16, cudaStream_t s) {
+  if (dtype == CA_DTYPE_BF16) {
+    switch (E) {
+      case 32: return launch_store_e<__nv_bfloat16, 32>(prm, vec16, s);
+      case 64: return launch_store_e<__nv_bfloat16, 64>(prm, vec16, s);
+      default: return launch_store_e<__nv_bfloat16, 128>(prm, vec16, s);
+    }
+  }
+  switch (E) {
+    case 32: return launch_store_e<float, 32>(prm, vec16, s);
+    case 64: return launch_store_e<float, 64>(prm, vec16, s);
+    default: return launch_store_e<float, 128>(prm, vec16, s);
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+int ca_store(const void* key, const void* value, int64_t token_stride, void* k_cache, void* v_cache,
+             int64_t num_blocks, const int64_t* slots, int64_t num_tokens, int64_t heads, int64_t head_dim,
+             int64_t page, int dtype, int32_t* status, void* stream) {
+  if (dtype != CA_DTYPE_F32 && dtype != CA_DTYPE_BF16) return CA_EDTYPE;
+  if (!head_dim_ok(head_dim)) return CA_EHEADDIM;
+  if (!page_ok(page)) return CA_EPAGE;
+  if (num_tokens < 0 || heads <= 0 || num_blocks < 0) return CA_ESHAPE;
+  if (num_tokens == 0) return CA_OK;
+  if (!key || !value || !k_cache || !v_cache || !slots) return CA_ENULL;
+  if (token_stride < heads * head_dim) return CA_ELAYOUT;
+  const size_t es = elem_size(dtype);
+  const bool vec16 = aligned(key, 16) && aligned(value, 16) && (token_stride * es) % 16 == 0;
+  if (!aligned(k_cache, es) || !aligned(v_cache, es) || !aligned(key, es) || !aligned(value, es))
+    return CA_ELAYOUT;
+  ca::StoreParams prm{};
+  prm.key = key;
+  prm.value = value;
+  prm.token_stride = token_stride;
+  prm.kc = k_cache;
+  prm.vc = v_cache;
+  prm.num_blocks = num_blocks;
+  prm.slots = reinterpret_cast<const long long*>(slots);
+  prm.tokens = num_tokens;
+  prm.H = (int)heads;
+  prm.page = (int)page;
+  prm.status = status;
+  return launch_store(prm, head_dim, dtype, vec16, static_cast<cudaStream_t>(stream));
+}
+
+size_t ca_decode_workspace_bytes(int64_t batch, int64_t heads, int64_t head_dim, int64_t page, int dtype,
+                                 int device) {
+  DeviceInfo dev;
+  if (device_info(device, &dev) != CA_OK) return 0;
+  DecodePlan pl;
+  if (!head_dim_ok(head_dim) || !page_ok(page) || !decode_plan(head_dim, page, dtype, dev, &pl)) return 0;
+  return decode_ws_bytes(batch, heads, dev);
+}
+
+int ca_decode(const void* q, int64_t q_stride, void* k_cache, void* v_cache, int64_t num_blocks,
+              const void* k_new, const void* v_new, int64_t kv_stride, const int64_t* slots, const int32_t* lens,
+              const int32_t* page_table, int64_t table_width, void* out, int64_t batch, int64_t heads,
+              int64_t head_dim, int64_t page, int dtype, float softmax_scale, void* workspace,
+              size_t workspace_bytes, void* stream) {
+  if (dtype != CA_DTYPE_F32 && dtype != CA_DTYPE_BF16) return CA_EDTYPE;
+  if (!head_dim_ok(head_dim)) return CA_EHEADDIM;
+  if (!page_ok(page)) return CA_EPAGE;
+  if (batch < 0 || heads <= 0 || num_blocks < 0 || table_width < 0) return CA_ESHAPE;
+  if ((k_new == nullptr) != (v_new == nullptr)) return CA_ESHAPE;
+  if (slots && !k_new) return CA_ESHAPE;  // `_C.mojo:140-143`
+  if (batch == 0) return CA_OK;
+  if (!q || !k_cache || !v_cache || !lens || !page_table || !out || !workspace) return CA_ENULL;
+  if (q_stride < heads * head_dim) return CA_ELAYOUT;
+  if (k_new && kv_stride < heads * head_dim) return CA_ELAYOUT;
+  // whole pages move by 16-byte bulk copies
+  if (!aligned(k_cache, 16) || !aligned(v_cache, 16)) return CA_ELAYOUT;
+  const size_t es = elem_size(dtype);
+  if (!aligned(q, es) || !aligned(out, es)) return CA_ELAYOUT;
+  int device;
+  int rc = current_device(&device);
+  if (rc) return rc;
+  DeviceInfo dev;
+  if ((rc = device_info(device, &dev))) return rc;
+  DecodePlan pl;
+  if (!decode_plan(head_dim, page, dtype, dev, &pl)) return CA_EUNSUPPORTED;
+  if (workspace_bytes < decode_ws_bytes(batch, heads, dev)) return CA_EWORKSPACE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  int32_t* status = reinterpret_cast<int32_t*>(ws);
+  float* partial = reinterpret_cast<float*>(ws + 256);
+  int32_t* tickets = reinterpret_cast<int32_t*>(ws + 256 + decode_partial_bytes(dev));
+
+  if (k_new) {
+    if (!aligned(k_new, es) || !aligned(v_new, es)) return CA_ELAYOUT;
+    ca::StoreParams sp{};
+    sp.key = k_new;
+    sp.value = v_new;
+    sp.token_stride = kv_stride;
+    sp.kc = k_cache;
+    sp.vc = v_cache;
+    sp.num_blocks = num_blocks;
+    sp.slots = reinterpret_cast<const long long*>(slots);
+    sp.lens = lens;
+    sp.page_table = page_table;
+    sp.pt_stride = table_width;
+    sp.tokens = batch;
+    sp.H = (int)heads;
+    sp.page = (int)page;
+    sp.status = status;
+    const bool vec16 = aligned(k_new, 16) && aligned(v_new, 16) && (kv_stride * es) % 16 == 0;
+    if ((rc = launch_store(sp, head_dim, dtype, vec16, s))) return rc;
+  }
+
+  ca::DecodeParams prm{};
+  prm.q = q;
+  prm.q_stride = q_stride;
+  prm.kc = k_cache;
+  prm.vc = v_cache;
+  prm.num_blocks = num_blocks;
+  prm.lens = lens;
+  prm.extra = (k_new && !slots) ? 1 : 0;
+  prm.page_table = page_table;
+  prm.pt_stride = table_width;
+  prm.out = out;
+  prm.out_stride = heads * head_dim;
+  prm.B = (int)batch;
+  prm.H = (int)heads;
+  prm.page = (int)page;
+  const double scale = std::isnan(softmax_scale) ? 1.0 / std::sqrt((double)head_dim) : (double)softmax_scale;
+  prm.c = (float)(scale * 1.4426950408889634);
+  prm.cp = pl.cp;
+  prm.stages = pl.stages;
+  prm.warp_bytes = pl.warp_bytes;
+  prm.stage_bytes = pl.stage_bytes;
+  prm.kslot_bytes = pl.kslot_bytes;
+  prm.page_bytes = pl.page_bytes;
+  prm.warps = pl.warps;
+  prm.partial = partial;
+  prm.tickets = tickets;
+  prm.status = status;
+  if (dtype == CA_DTYPE_BF16) return dispatch_decode<__nv_bfloat16>(head_dim, prm, pl, s, device);
+  return dispatch_decode<float>(head_dim, prm, pl, s, device);
+}
+
+int ca_flash(const void* q, const void* k, const void* v, void* out, int64_t batch, int64_t seq_q, int64_t seq_k,
+             int64_t heads, int64_t head_dim, const int64_t q_strides[3], const int64_t k_strides[3],
+             const int64_t v_strides[3], float softmax_scale, int causal, int dtype, void* stream) {
+  if (dtype != CA_DTYPE_F32 && dtype != CA_DTYPE_BF16) return CA_EDTYPE;
+  if (!head_dim_ok(head_dim)) return CA_EHEADDIM;
+  if (batch < 0 || seq_q < 1 || seq_k < 1 || heads <= 0) return CA_ESHAPE;
+  if (batch == 0) return CA_OK;
+  if (!q || !k || !v || !out || !q_strides || !k_strides || !v_strides) return CA_ENULL;
+  const size_t es = elem_size(dtype);
+  if (!aligned(q, es) || !aligned(k, es) || !aligned(v, es) || !aligned(out, es)) return CA_ELAYOUT;
+  const double scale = std::isnan(softmax_scale) ? 1.0 / std::sqrt((double)head_dim) : (double)softmax_scale;
+  ca::FlashParams prm{};
+  prm.q = q;
+  prm.k = k;
+  prm.v = v;
+  prm.out = out;
+  prm.B = (int)batch;
+  prm.Lq = (int)seq_q;
+  prm.Lk = (int)seq_k;
+  prm.H = (int)heads;
+  for (int i = 0; i < 3; ++i) {
+    prm.qs[i] = q_strides[i];
+    prm.ks[i] = k_strides[i];
+    prm.vs[i] = v_strides[i];
+  }
+  prm.c = (float)(scale * 1.4426950408889634);
+  prm.causal = causal ? 1 : 0;
+  int device;
+  int rc = current_device(&device);
+  if (rc) return rc;
+  DeviceInfo dev;
+  if ((rc = device_info(device, &dev))) return rc;
+  return ca::flash_launch(prm, (int)head_dim, dtype, dev.sms, static_cast<cudaStream_t>(stream), &g_cuda_error);
+}
+
+int ca_status(void* workspace, int reset, void* stream) {
+  if (!workspace) return CA_ENULL;
+  int32_t host = 0;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemcpyAsync(&host, workspace, 4, cudaMemcpyDeviceToHost, s);
+  if (e != cudaSuccess) return cuda_fail(e, "status read");
+  if (reset) {
+    e = cudaMemsetAsync(workspace, 0, 4, s);
+    if (e != cudaSuccess) return cuda_fail(e, "status reset");
+  }
+  e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_fail(e, "status sync");
+  return host;
+}
+
+const char* ca_last_cuda_error(void) { return g_cuda_error.c_str(); }
+
+const char* ca_build_info(void) {
+  static char info[96];
+  std::snprintf(info, sizeof(info), "sm_100a cuda %d.%d", CUDART_VERSION / 1000, (CUDART_VERSION % 1000) / 10);
+  return info;
+}
+
+}  // extern "C"

@@ -1,0 +1,143 @@
+/*
+ * cpu_attention_b200.h -- the C ABI of the B200 (sm_100a) build of cpu-attention.
+ *
+ * One shared object (libca_b200.so) replaces the reference's per-ISA-tier Mojo
+ * extensions (`cpu_attention/_kernel.py:52-84` loads one `_C_<tier>.so`). Its
+ * entries take plain device pointers, sizes and element strides; nothing in the
+ * signatures is a torch type, so any host language binds them (ctypes, cgo,
+ * JNI, N-API). Every compute entry is asynchronous on the caller's CUDA stream.
+ *
+ * Return convention (restates `_C.mojo:1-8`: "returns None for anything it does
+ * not take"): 0 = done; a negative CA_E* code = declined, nothing was launched,
+ * and the caller raises the precise error (the Python layer maps each code to
+ * the reference's ValueError / NotImplementedError text).
+ *
+ * Value errors that only the device can see (a cache_seqlens entry past the
+ * page table's capacity, a page-table entry or slot past the cache) never cause
+ * an out-of-bounds access: the kernels skip the offending work and OR a
+ * CA_STATUS_* bit into a status word in the workspace, read back with
+ * ca_status().
+ *
+ * dtype codes follow `_kernel.py:17` (DTYPES = {float32: 0, bfloat16: 1}).
+ */
+#ifndef CPU_ATTENTION_B200_H
+#define CPU_ATTENTION_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define CA_API __attribute__((visibility("default")))
+#else
+#define CA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- codes ------------------------------------------------------------ */
+#define CA_DTYPE_F32 0
+#define CA_DTYPE_BF16 1
+
+#define CA_OK 0
+#define CA_EDTYPE -1        /* dtype not fp32/bf16, or operands disagree      */
+#define CA_EHEADDIM -2      /* head_dim not 32/64/128                          */
+#define CA_EPAGE -3         /* page size not a positive multiple of 16         */
+#define CA_ESHAPE -4        /* sizes disagree (batch, heads, tokens, tables)   */
+#define CA_ELAYOUT -5       /* a stride/alignment the kernel cannot read       */
+#define CA_ENULL -6         /* a required pointer is NULL                      */
+#define CA_EWORKSPACE -7    /* workspace missing or too small                  */
+#define CA_ECUDA -8         /* a CUDA runtime call failed (ca_last_cuda_error) */
+#define CA_EUNSUPPORTED -9  /* a shape this build does not implement           */
+
+/* status bits written by the device into the workspace (ca_status) */
+#define CA_STATUS_LENS 1    /* cache_seqlens (+ the appended token) past W*page */
+#define CA_STATUS_TABLE 2   /* a page-table entry outside [0, num_blocks)      */
+#define CA_STATUS_SLOT 4    /* a slot_mapping entry >= num_blocks * page       */
+#define CA_STATUS_TIMEOUT 8 /* a bounded device wait gave up                   */
+
+/* ---- reshape_and_cache -------------------------------------------------
+ * Replaces `_C.store(rt, key, value, k_cache, v_cache, slots)` (`_C.mojo:174-213`)
+ * behind `cache.py:13-25` `reshape_and_cache`.
+ * key/value: [num_tokens, heads, head_dim] with heads and dims contiguous and
+ *   `token_stride` elements between tokens (both share it, `_C.mojo:198`).
+ * k_cache/v_cache: [num_blocks, heads, page, head_dim] contiguous, the reference's
+ *   in-page layout (`paged_attn.mojo:58-131`): K of token t, dim d at element
+ *   ((d>>1)*page + t)*2 + (d&1) (bf16) or d*page + t (fp32) of its (block, head)
+ *   page; V at t*head_dim + d.
+ * slots: int64 [num_tokens]; token i goes to page slots[i] / page, position
+ *   slots[i] % page; a negative slot skips the token (`paged_attn.mojo:155-158`).
+ *   Slots >= num_blocks*page are skipped and flagged (CA_STATUS_SLOT) in
+ *   `status` when it is non-NULL (a device int32).
+ */
+CA_API int ca_store(const void* key, const void* value, int64_t token_stride,
+             void* k_cache, void* v_cache, int64_t num_blocks,
+             const int64_t* slots, int64_t num_tokens, int64_t heads,
+             int64_t head_dim, int64_t page, int dtype, int32_t* status,
+             void* stream);
+
+/* ---- paged decode (flash_attn_with_kvcache, one query token) -----------
+ * Replaces `_C.decode(rt, q, k_cache, v_cache, k, v, slots, lens, page_table,
+ * scale, dst)` (`_C.mojo:87-171`), called by `flash_attn_interface.py:150-159`
+ * and by an engine directly (`examples/ops.py:19-31`).
+ * q: [batch, heads, head_dim] rows, heads and dims contiguous, `q_stride`
+ *   elements between sequences (any token stride: fused projections).
+ * k_new/v_new: NULL (cross-attention: no store), or the new token's K/V, same
+ *   row layout with `kv_stride` elements between sequences.
+ * slots: NULL = append each new token at position lens[i] through the page
+ *   table (`paged_attn.mojo:162-168`), and attend lens[i] + 1 keys; non-NULL =
+ *   store at slots[i] (int64, negative skips) and attend lens[i] keys
+ *   (`_C.mojo:100-103`, `paged_attn.mojo:723-725`).
+ * lens: int32 [batch]; page_table: int32 [batch, table_width] contiguous.
+ * out: [batch, heads, head_dim] contiguous (`_C.mojo:154-160`).
+ * softmax_scale: NaN selects the default head_dim ** -0.5 (`_C.mojo:168`).
+ * workspace: device memory of at least ca_decode_workspace_bytes() bytes,
+ *   zero-filled once before its first use; calls that overlap in time on the
+ *   device must not share one. A row that sees no key is exactly 0
+ *   (`paged_attn.mojo:297-310`).
+ */
+CA_API size_t ca_decode_workspace_bytes(int64_t batch, int64_t heads, int64_t head_dim,
+                                 int64_t page, int dtype, int device);
+
+CA_API int ca_decode(const void* q, int64_t q_stride, void* k_cache, void* v_cache,
+              int64_t num_blocks, const void* k_new, const void* v_new,
+              int64_t kv_stride, const int64_t* slots, const int32_t* lens,
+              const int32_t* page_table, int64_t table_width, void* out,
+              int64_t batch, int64_t heads, int64_t head_dim, int64_t page,
+              int dtype, float softmax_scale, void* workspace,
+              size_t workspace_bytes, void* stream);
+
+/* ---- dense prefill (flash_attn_func) ------------------------------------
+ * Replaces `_C.flash(rt, q, k, v, scale, causal, ws, ws_bytes)`
+ * (`_C.mojo:232-316`) behind `flash_attn_interface.py:168-193`.
+ * q: [batch, seq_q, heads, head_dim]; k/v: [batch, seq_k, heads, head_dim];
+ *   strides in elements (batch, token, head); the dim stride must be 1
+ *   (`_C.mojo:263`). out: [batch, seq_q, heads, head_dim] contiguous.
+ * causal: bottom-right aligned, row i sees keys j <= i + seq_k - seq_q; a row
+ *   that sees no key is exactly 0 (`flash_attn.mojo:127-183`).
+ * softmax_scale: NaN selects head_dim ** -0.5.
+ */
+CA_API int ca_flash(const void* q, const void* k, const void* v, void* out,
+             int64_t batch, int64_t seq_q, int64_t seq_k, int64_t heads,
+             int64_t head_dim, const int64_t q_strides[3],
+             const int64_t k_strides[3], const int64_t v_strides[3],
+             float softmax_scale, int causal, int dtype, void* stream);
+
+/* ---- runtime ------------------------------------------------------------ */
+/* The status word of a decode workspace (ORed CA_STATUS_* bits since the last
+ * reset); synchronises `stream`. reset != 0 clears it. Returns < 0 on a CUDA
+ * error. */
+CA_API int ca_status(void* workspace, int reset, void* stream);
+
+/* The last CUDA error string seen by this library on this host thread. */
+CA_API const char* ca_last_cuda_error(void);
+
+/* "sm_100a" plus the build's CUDA version, for diagnostics (the counterpart of
+ * `_C.tier()`, `_C.mojo:347-349`). */
+CA_API const char* ca_build_info(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CPU_ATTENTION_B200_H */

@@ -1,0 +1,182 @@
+"""The oracle, pinned before it is trusted (CPU only).
+
+* the numpy float64 restatement reproduces the reference's own float64 oracle
+  outputs (golden fixtures) on the reference's own test inputs;
+* the C restatement of the reference's CPU kernel passes the reference's gates
+  (`tests/reference.py:24-40`) on every golden case, and the reference's known
+  answers: a zero-length context is exactly 0, a row that sees no key is 0,
+  negative slots skip, NaN in unused slots never leaks;
+* the numpy layout restatement and the C store agree byte for byte, and with
+  the layout formulas of `paged_attn.mojo:76-113` element by element.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import cases
+from helpers import golden, stage_cache
+from oracle import attention_f64 as F64
+from oracle import cpu, paged
+
+
+def _bf(dtype):
+    return dtype == torch.bfloat16
+
+
+# ---------------------------------------------------------------- digests --
+def test_flash_inputs_match_golden_digests():
+    g = golden("flash")
+    for name, b, sq, sk, h, d, dtype, causal, seed, scale in cases.flash_cases():
+        q, k, v = cases.flash_inputs(b, sq, sk, h, d, dtype, seed)
+        assert str(g[name + "__digest"]) == cases.digest(q, k, v), name
+
+
+def test_decode_inputs_match_golden_digests():
+    g = golden("decode")
+    for name, lens, h, d, page, dtype, seed, scale in cases.decode_cases():
+        q, bt, total, ks, vs = cases.stage_inputs(lens, h, d, page, dtype, seed)
+        assert str(g[name + "__digest"]) == cases.digest(q, bt, *ks, *vs), name
+
+
+# ------------------------------------------------------ float64 restatement --
+@pytest.mark.parametrize("case", cases.flash_cases(), ids=lambda c: c[0])
+def test_f64_oracle_flash_matches_golden(case):
+    name, b, sq, sk, h, d, dtype, causal, seed, scale = case
+    q, k, v = cases.flash_inputs(b, sq, sk, h, d, dtype, seed)
+    got = F64.attention(q, k, v, scale or d ** -0.5, causal)
+    np.testing.assert_allclose(got, golden("flash")[name], rtol=0, atol=1e-12)
+
+
+def test_f64_oracle_decode_matches_golden():
+    for name, lens, h, d, page, dtype, seed, scale in cases.decode_cases():
+        q, bt, total, ks, vs = cases.stage_inputs(lens, h, d, page, dtype, seed)
+        got = np.concatenate([F64.attention(q[i:i + 1], ks[i], vs[i], scale or d ** -0.5)
+                              for i in range(len(lens))])
+        np.testing.assert_allclose(got, golden("decode")[name], rtol=0, atol=1e-12, err_msg=name)
+
+
+def test_f64_oracle_fully_masked_row_is_zero():
+    q = torch.randn(1, 5, 1, 32)
+    k = torch.randn(1, 2, 1, 32)
+    out = F64.attention(q, k, k, 0.2, causal=True)  # rows 0..2 see no key (5 > 2)
+    assert np.all(out[0, :3] == 0) and np.all(np.isfinite(out))
+
+
+# ------------------------------------------------------------ C restatement --
+def _cpu_store(key, value, kc, vc, slots):
+    cpu.store(key.contiguous(), value.contiguous(), kc, vc, slots.contiguous())
+
+
+@pytest.mark.parametrize("case", cases.decode_cases(), ids=lambda c: c[0])
+def test_c_oracle_decode_passes_reference_gates(case):
+    name, lens, h, d, page, dtype, seed, scale = case
+    q, kc, vc, bt, ks, vs = stage_cache(lens, h, d, page, dtype, seed, _cpu_store)
+    out = torch.empty(len(lens), h, d, dtype=dtype)
+    cpu.decode(q[:, 0], kc, vc, torch.tensor(lens, dtype=torch.int32), bt, out, scale=scale)
+    ref = golden("decode")[name][:, 0]
+    err, tol = F64.check(out, ref, _bf(dtype), paged=True)
+    assert err <= tol, (name, err)
+    zero = [i for i, n in enumerate(lens) if n == 0]
+    assert all(torch.all(out[i] == 0) for i in zero)  # zero-length context: exactly 0
+
+
+@pytest.mark.parametrize("case", cases.flash_cases(), ids=lambda c: c[0])
+def test_c_oracle_flash_passes_reference_gates(case):
+    name, b, sq, sk, h, d, dtype, causal, seed, scale = case
+    q, k, v = cases.flash_inputs(b, sq, sk, h, d, dtype, seed)
+    out = torch.empty(b, sq, h, d, dtype=dtype)
+    cpu.flash(q, k, v, out, scale=scale, causal=causal)
+    err, tol = F64.check(out, golden("flash")[name], _bf(dtype))
+    assert err <= tol, (name, err)
+
+
+def test_c_oracle_flash_strided_views():
+    """q/k/v as chunks of one fused [b, s, 3*h*d] projection (test_flash.py:39-47)."""
+    b, s, h, d = 2, 70, 4, 64
+    qkv = torch.randn(b, s, 3 * h * d, generator=torch.Generator().manual_seed(5))
+    q, k, v = (qkv[..., i * h * d:(i + 1) * h * d].view(b, s, h, d) for i in range(3))
+    out = torch.empty(b, s, h, d)
+    cpu.flash(q, k, v, out, causal=True)
+    err, tol = F64.check(out, F64.attention(q, k, v, d ** -0.5, True), False)
+    assert err <= tol
+
+
+def test_c_oracle_decode_append_equals_store_then_decode():
+    """Appending one token in the decode call writes the same cache as
+    reshape_and_cache at that slot (test_kvcache.py:143-161)."""
+    lens, h, d, page = [5, 31, 64], 4, 64, 16
+    for dtype in cases.DTYPES:
+        q, kc, vc, bt, ks, vs = stage_cache(lens, h, d, page, dtype, 3, _cpu_store)
+        kn, vn = (torch.randn(len(lens), h, d, generator=torch.Generator().manual_seed(i)).to(dtype)
+                  for i in range(2))
+        kc2, vc2 = kc.clone(), vc.clone()
+        out = torch.empty(len(lens), h, d, dtype=dtype)
+        cpu.decode(q[:, 0], kc, vc, torch.tensor(lens, dtype=torch.int32), bt, out, k_new=kn, v_new=vn)
+        slots = torch.tensor([int(bt[i, n // page]) * page + n % page for i, n in enumerate(lens)])
+        cpu.store(kn, vn, kc2, vc2, slots)
+        assert np.array_equal(kc.view(torch.int16 if dtype == torch.bfloat16 else torch.int32).numpy(),
+                              kc2.view(torch.int16 if dtype == torch.bfloat16 else torch.int32).numpy())
+        ref = np.concatenate([F64.attention(q[i:i + 1], torch.cat([ks[i], kn[i:i + 1, None]], 1),
+                                            torch.cat([vs[i], vn[i:i + 1, None]], 1), d ** -0.5)
+                              for i in range(len(lens))])
+        err, tol = F64.check(out, ref[:, 0], dtype == torch.bfloat16, paged=True)
+        assert err <= tol
+
+
+# ------------------------------------------------------------------ layout --
+@pytest.mark.parametrize("bf16", [True, False])
+@pytest.mark.parametrize("page", [16, 48])
+def test_layout_numpy_equals_c_store_and_formula(bf16, page):
+    rng = np.random.default_rng(7)
+    nb, h, d, n = 5, 3, 64, 40
+    et = np.uint16 if bf16 else np.float32
+    key = rng.integers(0, 2 ** 15, size=(n, h, d)).astype(et) if bf16 else rng.standard_normal((n, h, d)).astype(et)
+    val = rng.integers(0, 2 ** 15, size=(n, h, d)).astype(et) if bf16 else rng.standard_normal((n, h, d)).astype(et)
+    slots = rng.permutation(nb * page)[:n].astype(np.int64)
+    slots[3] = -1  # skipped
+    kc = np.zeros((nb, h, page, d), et)
+    vc = np.zeros_like(kc)
+    paged.store(kc, vc, key, val, slots)
+    kc2, vc2 = np.zeros_like(kc), np.zeros_like(vc)
+    cpu.store(key, val, kc2, vc2, slots)
+    assert np.array_equal(kc.view(np.uint8), kc2.view(np.uint8))
+    assert np.array_equal(vc.view(np.uint8), vc2.view(np.uint8))
+    # element by element, straight from the formulas
+    flat = kc.reshape(nb, h, page * d)
+    for i, s in enumerate(slots):
+        if s < 0:
+            continue
+        blk, off = divmod(int(s), page)
+        for hh in range(h):
+            for dd in range(d):
+                o = ((dd >> 1) * page + off) * 2 + (dd & 1) if bf16 else dd * page + off
+                assert flat[blk, hh, o] == key[i, hh, dd]
+                assert vc[blk, hh, off, dd] == val[i, hh, dd]
+    # the skipped token left its zeros
+    assert np.count_nonzero(vc) == (n - 1) * h * d or not bf16
+
+
+def test_exp2_polynomials_error_bounds():
+    """The documented errors of the reference's exp2 (isa.mojo:86-89), as
+    restated in ca_oracle.c, via the decode of a one-key-vs-two-key case."""
+    # exp2 itself is internal to the C file; check it through softmax weights:
+    # two keys with logit gap g give weights 1/(1+2^-g) -- compare to float64.
+    d, h, page = 32, 1, 16
+    q = torch.zeros(1, 1, d)
+    q[0, 0, 0] = 1.0
+    kc = torch.zeros(1, h, page, d)
+    vc = torch.zeros(1, h, page, d)
+    gaps = [0.1, 0.7, 1.3, 3.9]
+    for g in gaps:
+        key = torch.zeros(2, 1, d)
+        key[0, 0, 0] = g / (d ** -0.5 * 1.4426950408889634)
+        val = torch.zeros(2, 1, d)
+        val[0, 0, 1] = 1.0
+        val[1, 0, 2] = 1.0
+        cpu.store(key, val, kc, vc, torch.tensor([0, 1]))
+        out = torch.empty(1, 1, d)
+        cpu.decode(q, kc, vc, torch.tensor([2], dtype=torch.int32), torch.zeros(1, 1, dtype=torch.int32), out)
+        w = 1.0 / (1.0 + 2.0 ** -g)
+        assert abs(out[0, 0, 1].item() - w) < 1e-6
+        assert abs(out[0, 0, 2].item() - (1 - w)) < 1e-6
