@@ -174,9 +174,10 @@ def flash(rt, q, k, v, scale, causal):
         return out
     stream = torch.cuda.current_stream(dev).cuda_stream
     arr = (K.i64x3(q.stride()[:3]), K.i64x3(k.stride()[:3]), K.i64x3(v.stride()[:3]))
+    ws = K.workspace(dev, stream)
     with K.on_device(dev):
         rc = K.library().ca_flash(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), b, sq, sk, heads, hd,
-                                  *arr, _scale(scale), int(causal), dt, stream)
+                                  *arr, _scale(scale), int(causal), dt, ws.data_ptr(), stream)
     if not _check_rc(rc):
         return None
     return out

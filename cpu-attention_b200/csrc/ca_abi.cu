@@ -10,6 +10,7 @@
 
 #include "decode.cuh"
 #include "flash.cuh"
+#include "flash_tc.cuh"
 #include "store.cuh"
 
 namespace {
@@ -287,7 +288,8 @@ int ca_decode(const void* q, int64_t q_stride, void* k_cache, void* v_cache, int
 
 int ca_flash(const void* q, const void* k, const void* v, void* out, int64_t batch, int64_t seq_q, int64_t seq_k,
              int64_t heads, int64_t head_dim, const int64_t q_strides[3], const int64_t k_strides[3],
-             const int64_t v_strides[3], float softmax_scale, int causal, int dtype, void* stream) {
+             const int64_t v_strides[3], float softmax_scale, int causal, int dtype, int32_t* status,
+             void* stream) {
   if (dtype != CA_DTYPE_F32 && dtype != CA_DTYPE_BF16) return CA_EDTYPE;
   if (!head_dim_ok(head_dim)) return CA_EHEADDIM;
   if (batch < 0 || seq_q < 1 || seq_k < 1 || heads <= 0) return CA_ESHAPE;
@@ -317,7 +319,7 @@ int ca_flash(const void* q, const void* k, const void* v, void* out, int64_t bat
   if (rc) return rc;
   DeviceInfo dev;
   if ((rc = device_info(device, &dev))) return rc;
-  return ca::flash_launch(prm, (int)head_dim, dtype, dev.sms, static_cast<cudaStream_t>(stream), &g_cuda_error);
+  return ca::flash_launch(prm, (int)head_dim, dtype, status, static_cast<cudaStream_t>(stream), &g_cuda_error);
 }
 
 int ca_status(void* workspace, int reset, void* stream) {

@@ -202,9 +202,21 @@ int flash_generic_launch(const FlashParams& p, cudaStream_t stream, std::string*
   return CA_OK;
 }
 
-inline int flash_launch(const FlashParams& p, int E, int dtype, int sms, cudaStream_t stream, std::string* err) {
-  (void)sms;
+template <int E>
+int flash_tc_launch(const FlashParams& p, int* status, cudaStream_t stream, std::string* err);
+
+// bf16 runs on the tensor cores (tcgen05) whenever TMA can describe q/k/v;
+// fp32 (and bf16 layouts TMA cannot describe) on the CUDA-core kernel.
+inline int flash_launch(const FlashParams& p, int E, int dtype, int* status, cudaStream_t stream,
+                        std::string* err) {
   if (dtype == CA_DTYPE_BF16) {
+    int rc = CA_EUNSUPPORTED;
+    switch (E) {
+      case 32: rc = flash_tc_launch<32>(p, status, stream, err); break;
+      case 64: rc = flash_tc_launch<64>(p, status, stream, err); break;
+      default: rc = flash_tc_launch<128>(p, status, stream, err); break;
+    }
+    if (rc != CA_EUNSUPPORTED) return rc;
     switch (E) {
       case 32: return flash_generic_launch<__nv_bfloat16, 32>(p, stream, err);
       case 64: return flash_generic_launch<__nv_bfloat16, 64>(p, stream, err);

@@ -105,7 +105,7 @@ constexpr uint32_t kSwizzle128 = 2, kSwizzle64 = 4;
 
 // Instruction descriptor, kind::f16: fp32 accumulator, bf16 A and B,
 // A K-major, B K-major (b_mn = 0) or MN-major (b_mn = 1), M x N.
-constexpr uint32_t idesc_bf16(int M, int N, int b_mn) {
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, int b_mn) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)b_mn << 16) | ((uint32_t)(N >> 3) << 17) |
          ((uint32_t)(M >> 4) << 24);
 }

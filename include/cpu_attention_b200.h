@@ -117,12 +117,18 @@ CA_API int ca_decode(const void* q, int64_t q_stride, void* k_cache, void* v_cac
  * causal: bottom-right aligned, row i sees keys j <= i + seq_k - seq_q; a row
  *   that sees no key is exactly 0 (`flash_attn.mojo:127-183`).
  * softmax_scale: NaN selects head_dim ** -0.5.
+ * status: NULL, or a device int32 that receives CA_STATUS_TIMEOUT if a
+ *   bounded device wait gives up.
+ * bf16 runs on the tensor cores (tcgen05, TMA-fed) whenever TMA can describe
+ * q/k/v (16-byte aligned base and strides); fp32 and other bf16 layouts run on
+ * a CUDA-core kernel.
  */
 CA_API int ca_flash(const void* q, const void* k, const void* v, void* out,
              int64_t batch, int64_t seq_q, int64_t seq_k, int64_t heads,
              int64_t head_dim, const int64_t q_strides[3],
              const int64_t k_strides[3], const int64_t v_strides[3],
-             float softmax_scale, int causal, int dtype, void* stream);
+             float softmax_scale, int causal, int dtype, int32_t* status,
+             void* stream);
 
 /* ---- runtime ------------------------------------------------------------ */
 /* The status word of a decode workspace (ORed CA_STATUS_* bits since the last

@@ -169,9 +169,9 @@ def test_abi_declines_bad_arguments_without_a_device():
     assert dec(q_stride=100) == K.ELAYOUT
     assert dec(b=0) == K.OK  # nothing to do
     st = (ctypes.c_int64 * 3)(0, 0, 0)
-    assert lib.ca_flash(p, p, p, p, 1, 4, 4, 2, 48, st, st, st, 1.0, 1, 0, None) == K.EHEADDIM
-    assert lib.ca_flash(p, p, p, p, 1, 0, 4, 2, 64, st, st, st, 1.0, 1, 0, None) == K.ESHAPE
-    assert lib.ca_flash(p, p, p, p, 1, 4, 4, 2, 64, st, st, st, 1.0, 1, 3, None) == K.EDTYPE
+    assert lib.ca_flash(p, p, p, p, 1, 4, 4, 2, 48, st, st, st, 1.0, 1, 0, None, None) == K.EHEADDIM
+    assert lib.ca_flash(p, p, p, p, 1, 0, 4, 2, 64, st, st, st, 1.0, 1, 0, None, None) == K.ESHAPE
+    assert lib.ca_flash(p, p, p, p, 1, 4, 4, 2, 64, st, st, st, 1.0, 1, 3, None, None) == K.EDTYPE
     assert lib.ca_store(p, p, 128, p, p, 4, p, 3, 2, 64, 12, 0, None, None) == K.EPAGE
     assert lib.ca_store(p, p, 100, p, p, 4, p, 3, 2, 64, 16, 0, None, None) == K.ELAYOUT
     assert lib.ca_store(p, p, 128, p, p, 4, p, 0, 2, 64, 16, 0, None, None) == K.OK
