@@ -2,7 +2,8 @@
 
     python cpu-attention_b200/build.py [--force] [--verbose]
 
-One nvcc invocation: csrc/ca_abi.cu (which includes every kernel) ->
+One nvcc invocation: csrc/ca_abi.cu (which includes every kernel) and
+csrc/ca_noalloc.cu (the allocation-free decode entry) ->
 cpu_attention/libca_b200.so, compiled for sm_100a only, with line info, static
 CUDA runtime. Rebuilds only when a source or this script is newer than the
 library. nvcc cross-compiles, so this runs on a machine without a GPU.
@@ -50,7 +51,7 @@ def build(force=False, verbose=False):
     if not force and not stale():
         return OUT
     tmp = OUT + ".tmp"
-    cmd = [nvcc(), *ARCH, *FLAGS, "-o", tmp, os.path.join(CSRC, "ca_abi.cu")]
+    cmd = [nvcc(), *ARCH, *FLAGS, "-o", tmp, os.path.join(CSRC, "ca_abi.cu"), os.path.join(CSRC, "ca_noalloc.cu")]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
         print(" ".join(cmd), flush=True)

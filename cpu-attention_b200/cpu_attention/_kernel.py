@@ -26,8 +26,8 @@ _DIR = os.path.dirname(os.path.abspath(__file__))
 LIB_NAME = "libca_b200.so"
 
 # return codes and device status bits (include/cpu_attention_b200.h)
-OK, EDTYPE, EHEADDIM, EPAGE, ESHAPE, ELAYOUT, ENULL, EWORKSPACE, ECUDA, EUNSUPPORTED = (
-    0, -1, -2, -3, -4, -5, -6, -7, -8, -9)
+OK, EDTYPE, EHEADDIM, EPAGE, ESHAPE, ELAYOUT, ENULL, EWORKSPACE, ECUDA, EUNSUPPORTED, ESCRATCH = (
+    0, -1, -2, -3, -4, -5, -6, -7, -8, -9, -10)
 STATUS_LENS, STATUS_TABLE, STATUS_SLOT, STATUS_TIMEOUT = 1, 2, 4, 8
 
 # Every exported symbol the header declares, with its ctypes signature.
@@ -39,6 +39,8 @@ SIGNATURES = {
     "ca_decode_workspace_bytes": (_SZ, [_I64, _I64, _I64, _I64, _I32, _I32]),
     "ca_decode": (_I32, [_P, _I64, _P, _P, _I64, _P, _P, _I64, _P, _P, _P, _I64, _P,
                          _I64, _I64, _I64, _I64, _I32, _F, _P, _SZ, _P]),
+    "ca_decode_noalloc": (_I32, [_P, _I64, _P, _P, _I64, _P, _P, _I64, _P, _P, _P, _I64, _P,
+                                 _I64, _I64, _I64, _I64, _I32, _F, _P]),
     "ca_flash": (_I32, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _PI64, _PI64, _PI64, _F, _I32, _I32, _P,
                         _P]),
     "ca_status": (_I32, [_P, _I32, _P]),

@@ -50,6 +50,7 @@ extern "C" {
 #define CA_EWORKSPACE -7    /* workspace missing or too small                  */
 #define CA_ECUDA -8         /* a CUDA runtime call failed (ca_last_cuda_error) */
 #define CA_EUNSUPPORTED -9  /* a shape this build does not implement           */
+#define CA_ESCRATCH -10     /* beyond ca_decode_noalloc's static scratch        */
 
 /* status bits written by the device into the workspace (ca_status) */
 #define CA_STATUS_LENS 1    /* cache_seqlens (+ the appended token) past W*page */
@@ -107,6 +108,29 @@ CA_API int ca_decode(const void* q, int64_t q_stride, void* k_cache, void* v_cac
               int64_t batch, int64_t heads, int64_t head_dim, int64_t page,
               int dtype, float softmax_scale, void* workspace,
               size_t workspace_bytes, void* stream);
+
+/* ---- paged decode without allocation -----------------------------------
+ * No counterpart in the reference: an addition for callers that cannot
+ * allocate device memory (an engine that reserves all GPU memory up front and
+ * forbids later allocations; a plugin interface that passes only input and
+ * output buffers). Same arguments and result as ca_decode, minus the
+ * workspace: it runs ca_decode with a static device array of the library as
+ * the workspace and allocates nothing.
+ * Limits: batch * heads <= 65536 and at most 160 SMs, else CA_ESCRATCH and
+ *   nothing is launched. The array (about 1.6 MiB) stays resident on every
+ *   GPU that loads the library until the process exits.
+ * Every call shares the array: calls that overlap on the GPU race; order them.
+ *   Device-found value errors are skipped but not reported (validate on the
+ *   host). The first call on a device looks up the array's address; make it
+ *   before any stream capture.
+ */
+CA_API int ca_decode_noalloc(const void* q, int64_t q_stride, void* k_cache,
+              void* v_cache, int64_t num_blocks, const void* k_new,
+              const void* v_new, int64_t kv_stride, const int64_t* slots,
+              const int32_t* lens, const int32_t* page_table,
+              int64_t table_width, void* out, int64_t batch, int64_t heads,
+              int64_t head_dim, int64_t page, int dtype, float softmax_scale,
+              void* stream);
 
 /* ---- dense prefill (flash_attn_func) ------------------------------------
  * Replaces `_C.flash(rt, q, k, v, scale, causal, ws, ws_bytes)`
