@@ -319,15 +319,23 @@ class ClockSampler:
         self.gpus = gpus
 
     def start(self):
+        """Start sampling every 50 ms; returns once the first sample is in
+        (at most ~5 s), so the timed region that follows is covered."""
         try:
             fd, self.path = tempfile.mkstemp(suffix=".csv")
             os.close(fd)
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={','.join(str(g) for g in self.gpus)}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.fh, stderr=subprocess.DEVNULL)
+                 "--format=csv,noheader,nounits", "-lms", "50"], stdout=self.fh, stderr=subprocess.DEVNULL)
         except (OSError, ValueError):
             self.proc = None
+            return
+        t0 = time.time()
+        while time.time() - t0 < 5.0:
+            if os.path.getsize(self.path) > 0:
+                break
+            time.sleep(0.02)
 
     def stop(self):
         if self.proc is None:
@@ -359,8 +367,16 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def timed(fn, steps, warmup, flush, stream):
-    """Per-step CUDA-event times (ms) on `stream`, L2 flushed before each step."""
+HOST_HIDE_CYCLES = 400_000  # ~0.2 ms of device spin: longer than the host needs to enqueue one step
+
+
+def timed(fn, steps, warmup, flush, stream, hide_host=True):
+    """Per-step CUDA-event times (ms) on `stream`, L2 flushed before each step.
+
+    With hide_host, a device-side spin follows the flush, so the device is
+    still busy when the host has enqueued the step: the events then bracket
+    the step's device work, not the host's enqueue latency (the e2e timing
+    runs without it: there the host's share belongs to the number)."""
     for _ in range(warmup):
         flush()
         fn()
@@ -368,6 +384,8 @@ def timed(fn, steps, warmup, flush, stream):
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     for a, b in evs:
         flush()
+        if hide_host:
+            torch.cuda._sleep(HOST_HIDE_CYCLES)
         a.record(stream)
         fn()
         b.record(stream)
@@ -488,6 +506,8 @@ def main():
     flush = lambda: flush_buf.fill_(1)  # noqa: E731
     metric, unit, scale = metric_of(wl)
 
+    # clocks are sampled from here through the roofline and e2e phases: the
+    # whole window in which this run keeps the GPUs busy
     barrier(world)
     sampler = ClockSampler(list(range(world))) if rank == 0 else None
     if sampler:
@@ -495,7 +515,6 @@ def main():
     barrier(world)
     step_ms = timed(wl.step, args.steps, args.warmup, flush, stream)
     barrier(world)
-    clocks = sampler.stop() if sampler else None
     total_ms = max_over_ranks(sum(step_ms), world)
     units = sum_over_ranks(wl.units(), world)
     ms_per_step = total_ms / args.steps
@@ -518,9 +537,11 @@ def main():
 
     # end to end through the public API, host buffers
     wl.e2e_setup()
-    e2e_ms = timed(wl.e2e_step, args.steps, 2, flush, stream)
+    e2e_ms = timed(wl.e2e_step, args.steps, 2, flush, stream, hide_host=False)
     e2e_total = max_over_ranks(sum(e2e_ms), world)
     e2e_value = units / (e2e_total / args.steps * 1e-3) / scale
+    barrier(world)
+    clocks = sampler.stop() if sampler else None
 
     line = {"metric": metric, "value": round(value, 3), "unit": unit, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "us_per_call": round(ms_per_step * 1e3, 2),

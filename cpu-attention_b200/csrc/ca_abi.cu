@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <cmath>
+#include <cstdlib>
 #include <cstdio>
 #include <mutex>
 #include <string>
@@ -56,47 +57,62 @@ int current_device(int* dev) {
 
 // ---- decode plan ---------------------------------------------------------
 struct DecodePlan {
-  int cp, stages, warps, stage_bytes, kslot_bytes, page_bytes, warp_bytes, smem_bytes, ctas;
+  int stages, warps, stage_bytes, kslot_bytes, page_bytes, warp_bytes, smem_bytes, ctas, pages_per_warp, task_cap, ahead, tail_div;
 };
 
-constexpr int kDecodeStageTarget = 16384;  // bytes of K+V per stage
-constexpr int kDecodeRingTarget = 49152;   // bytes of ring per warp
-constexpr int kDecodeMaxWarps = 8;
+constexpr int kDecodeRingTarget = 16384;  // bytes of ring per warp
+constexpr int kTasksPerSm = 32;           // split tasks per SM at most (task_cap / SMs)
+
+// CA_DECODE_STAGES / CA_DECODE_WARPS / CA_DECODE_PPW / CA_DECODE_AHEAD / CA_DECODE_TAILDIV override the plan (for
+// tuning sweeps); values that do not fit fall back to the defaults.
+int env_int(const char* name) {
+  const char* v = std::getenv(name);
+  return v ? std::atoi(v) : 0;
+}
+
+// Shared memory of the CTA-wide area behind the streaming warps' rings: the
+// task queue with its query rows, and the merge buffers.
+int decode_cta_extra(long long head_dim, int warps) { return ca::decode_cta_bytes((int)head_dim, warps); }
 
 bool decode_plan(long long head_dim, long long page, int dtype, const DeviceInfo& dev, DecodePlan* pl) {
+  if (page > ca::kDecodeMaxPage) return false;
+  static const int o_st = env_int("CA_DECODE_STAGES"), o_w = env_int("CA_DECODE_WARPS"),
+                   o_ppw = env_int("CA_DECODE_PPW"), o_ah = env_int("CA_DECODE_AHEAD"), o_td = env_int("CA_DECODE_TAILDIV");
   const long long page_bytes = page * head_dim * (long long)elem_size(dtype);
-  if (page > ca::kDecodeMaxChunkTokens) return false;
-  int cp = (int)std::max(1LL, std::min((long long)ca::kDecodeMaxChunkTokens / page,
-                                       (long long)kDecodeStageTarget / (2 * page_bytes)));
-  pl->cp = cp;
   pl->page_bytes = (int)page_bytes;
   pl->kslot_bytes = (int)page_bytes + ca::kKSlotPadBytes;
-  pl->stage_bytes = cp * (pl->kslot_bytes + (int)page_bytes);
-  const int extra = (int)(head_dim * 4 + ca::kDecodeMaxChunkTokens * 4);
+  pl->stage_bytes = pl->kslot_bytes + (int)page_bytes;
   const int budget = dev.max_smem_optin - 1024;
   int stages = std::max(2, std::min(4, kDecodeRingTarget / pl->stage_bytes));
-  auto warp_bytes = [&](int s) {
-    int w = s * pl->stage_bytes + extra + s * ((int)sizeof(ca::ChunkHdr) + 8);
-    return (w + 127) / 128 * 128;
-  };
-  while (stages > 2 && warp_bytes(stages) > budget) --stages;
-  if (warp_bytes(stages) > budget) return false;
+  if (o_st >= 2 && o_st <= 8) stages = o_st;
+  auto warp_bytes = [&](int s) { return ca::decode_warp_bytes(s, pl->stage_bytes); };
+  auto fits = [&](int s, int warps) { return warps * warp_bytes(s) + decode_cta_extra(head_dim, warps) <= budget; };
+  while (stages > 2 && !fits(stages, 1)) --stages;
+  if (!fits(stages, 1)) return false;
+  int warps = ca::kDecodeMaxWarps;
+  while (warps > 1 && !fits(stages, warps)) --warps;
+  if (o_w > 0 && o_w < warps) warps = o_w;
   pl->stages = stages;
+  pl->warps = warps;
   pl->warp_bytes = warp_bytes(stages);
-  pl->warps = std::max(1, std::min(kDecodeMaxWarps, budget / pl->warp_bytes));
-  pl->smem_bytes = pl->warps * pl->warp_bytes;
+  pl->smem_bytes = warps * pl->warp_bytes + decode_cta_extra(head_dim, warps);
   pl->ctas = dev.sms;
+  pl->pages_per_warp = (o_ppw > 0 && o_ppw <= 64) ? o_ppw : 4;
+  pl->task_cap = kTasksPerSm * dev.sms;
+  pl->ahead = (o_ah > 0 && o_ah <= 4096) ? o_ah : ca::kDecodeAhead;
+  pl->tail_div = (o_td > 0 && o_td <= 16) ? o_td : 2;
   return true;
 }
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-// workspace: [status int32 | pad to 256][partials: float, 2 slots per possible
-// worker warp, fixed per device][tickets: int32 per (sequence, head)]. The
-// tickets sit at a fixed offset so that no call's partials ever land on another
-// call's tickets, which must stay zero between calls.
+// workspace: [status int32, task counter int32 | pad to 256][partials: float,
+// 2 * task_cap + 2 slots of (E + 2), fixed per device][tickets: int32 per
+// (sequence, head)]. The tickets sit at a fixed offset so that no call's
+// partials ever land on another call's tickets; the counter and the tickets
+// are zero between calls (the kernel leaves them so).
 size_t decode_partial_bytes(const DeviceInfo& dev) {
-  return align256((size_t)2 * dev.sms * kDecodeMaxWarps * (128 + 2) * 4);
+  return align256((size_t)(2 * (size_t)kTasksPerSm * dev.sms + 2) * (128 + 2) * 4);
 }
 size_t decode_ws_bytes(long long batch, long long heads, const DeviceInfo& dev) {
   return 256 + decode_partial_bytes(dev) + align256((size_t)(batch * heads) * 4);
@@ -115,7 +131,7 @@ int launch_decode(const ca::DecodeParams& prm, const DecodePlan& pl, cudaStream_
       configured[device] = pl.smem_bytes;
     }
   }
-  kern<<<pl.ctas, 32 * pl.warps, pl.smem_bytes, stream>>>(prm);
+  kern<<<pl.ctas, 32 * (pl.warps + 2 + ca::kDecodeFinishers), pl.smem_bytes, stream>>>(prm);  // one persistent CTA per SM
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? CA_OK : cuda_fail(e, "decode launch");
 }
@@ -231,10 +247,14 @@ int ca_decode(const void* q, int64_t q_stride, void* k_cache, void* v_cache, int
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   char* ws = static_cast<char*>(workspace);
   int32_t* status = reinterpret_cast<int32_t*>(ws);
+  int32_t* counter = reinterpret_cast<int32_t*>(ws + 4);
   float* partial = reinterpret_cast<float*>(ws + 256);
   int32_t* tickets = reinterpret_cast<int32_t*>(ws + 256 + decode_partial_bytes(dev));
 
-  if (k_new) {
+  // By slot, the new tokens are stored first (a separate launch: a slot may
+  // lie anywhere). Appended at lens[i] through the page table, the decode
+  // kernel itself writes them (fused).
+  if (k_new && slots) {
     if (!aligned(k_new, es) || !aligned(v_new, es)) return CA_ELAYOUT;
     ca::StoreParams sp{};
     sp.key = k_new;
@@ -263,6 +283,10 @@ int ca_decode(const void* q, int64_t q_stride, void* k_cache, void* v_cache, int
   prm.num_blocks = num_blocks;
   prm.lens = lens;
   prm.extra = (k_new && !slots) ? 1 : 0;
+  prm.k_new = prm.extra ? k_new : nullptr;
+  prm.v_new = prm.extra ? v_new : nullptr;
+  prm.kv_stride = kv_stride;
+  prm.counter = counter;
   prm.page_table = page_table;
   prm.pt_stride = table_width;
   prm.out = out;
@@ -272,13 +296,16 @@ int ca_decode(const void* q, int64_t q_stride, void* k_cache, void* v_cache, int
   prm.page = (int)page;
   const double scale = std::isnan(softmax_scale) ? 1.0 / std::sqrt((double)head_dim) : (double)softmax_scale;
   prm.c = (float)(scale * 1.4426950408889634);
-  prm.cp = pl.cp;
   prm.stages = pl.stages;
   prm.warp_bytes = pl.warp_bytes;
   prm.stage_bytes = pl.stage_bytes;
   prm.kslot_bytes = pl.kslot_bytes;
   prm.page_bytes = pl.page_bytes;
   prm.warps = pl.warps;
+  prm.pages_per_warp = pl.pages_per_warp;
+  prm.ahead = pl.ahead;
+  prm.tail_div = pl.tail_div;
+  prm.task_cap = pl.task_cap;
   prm.partial = partial;
   prm.tickets = tickets;
   prm.status = status;

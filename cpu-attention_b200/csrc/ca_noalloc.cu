@@ -13,12 +13,13 @@
 //
 // Limits: batch * heads <= kMaxSeqHeads (65536) and at most kMaxSms (160)
 // SMs on the device; beyond either the call returns CA_ESCRATCH and launches
-// nothing. The array (about 1.6 MiB) is held by every GPU that loads the
+// nothing. The array (about 5.3 MiB) is held by every GPU that loads the
 // library, until the process exits.
 //
 // The array is shared by every call on a device and keeps the last call's
 // contents: each call first clears, on its stream, the words that must start
-// at zero (the status word and the tickets of its batch). Calls whose work
+// at zero (the status word, the task counter and the tickets of its
+// batch). Calls whose work
 // overlaps on the GPU (different streams, no ordering) race on it; order them.
 // Value errors the device finds (lengths past the page table, table entries
 // or slots past the cache) are skipped as in ca_decode but recorded only in the
@@ -38,11 +39,12 @@ namespace {
 
 constexpr long long kMaxSeqHeads = 65536;
 constexpr int kMaxSms = 160;
-constexpr int kMaxWarps = 8;  // decode worker warps per CTA at most (ca_abi.cu)
+constexpr int kTasksPerSm = 32;  // split tasks per SM at most (ca_abi.cu)
 constexpr size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
-// status word | split-merge partials of the largest grid | tickets
-constexpr size_t kScratchBytes =
-    256 + align256((size_t)2 * kMaxSms * kMaxWarps * (128 + 2) * 4) + align256((size_t)kMaxSeqHeads * 4);
+// status word and task counter | split-task partials of the largest grid (the
+// layout of ca_decode's workspace) | tickets
+constexpr size_t kScratchBytes = 256 + align256((size_t)(2 * (size_t)kTasksPerSm * kMaxSms + 2) * (128 + 2) * 4) +
+                                 align256((size_t)kMaxSeqHeads * 4);
 
 static __device__ __align__(256) unsigned char g_decode_scratch[kScratchBytes];
 
@@ -86,7 +88,7 @@ extern "C" int ca_decode_noalloc(const void* q, int64_t q_stride, void* k_cache,
     // tickets are the last align256(batch*heads*4) bytes of the workspace
     const size_t tickets = need - align256((size_t)(batch * heads) * 4);
     char* base = static_cast<char*>(scratch);
-    if (cudaMemsetAsync(base, 0, 4, s) != cudaSuccess ||
+    if (cudaMemsetAsync(base, 0, 8, s) != cudaSuccess ||
         cudaMemsetAsync(base + tickets, 0, (size_t)(batch * heads) * 4, s) != cudaSuccess)
       return CA_ECUDA;
   }

@@ -74,6 +74,9 @@ __device__ __forceinline__ void fence_barrier_init() {
 
 // Orders this thread's generic-proxy shared-memory accesses before later
 // async-proxy (bulk copy) accesses.
+// Release/acquire fence at GPU scope (lighter than __threadfence's fence.sc).
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

@@ -7,36 +7,66 @@
 //     x_t = (q . k_t) * scale * log2(e)          (fp32, exact bf16 products)
 //     m   = max_t x_t,  p_t = 2^(x_t - m),  l = sum_t p_t
 //     out = (sum_t p_t v_t) * (1 / l)           (0 when l == 0, `:297-310`)
-// computed with FlashAttention's online softmax in log2 units.
+// computed page by page in log2 units and combined with FlashAttention's
+// rescaling, always in page order, so the result does not depend on which
+// warp or SM streamed which page (it is bitwise reproducible).
 //
 // How it runs on the B200 (nothing here is a translation of the CPU drivers):
-//   * Work is measured in "units": one unit per cached page of an item plus one
-//     fixed-cost unit per item -- the reference's own cost model (`_share`,
-//     `paged_attn.mojo:788-816`: context + one 16-key unit per item). Item
-//     (i, h) owns units [U_ih, U_ih + np_i + 1). Every worker warp of a
-//     persistent grid takes one contiguous range [floor(kP/G), floor((k+1)P/G))
-//     of the P units, so all warps stream the same number of pages; an item
-//     cut by a range boundary becomes "pieces" whose partial softmax states
-//     (m, l, acc) are merged by whichever piece finishes last (an atomic
-//     ticket; nobody waits on anybody).
-//   * Each warp is its own producer: it keeps a ring of S stages in shared
-//     memory and fills each stage with whole (block, head) pages of K and V
-//     by 1-D bulk copies (cp.async.bulk, the TMA engine), S-1 chunks ahead of
-//     the chunk it computes, completing on one mbarrier per stage.
-//   * Q.K^T: lane = key (32 keys per step), reading the dim-pair-major K page
-//     with conflict-free 32-bit shared loads and the fp32 query as broadcast
-//     float4 loads. P.V: lanes own 4 dims of a V row (E/4 lanes per key).
+//   * Work is cut into tasks: a task is a run of consecutive pages of one
+//     item (sequence i, head h), the item's pages split evenly into
+//     ceil(np / U) tasks, numbered in (sequence, head, piece) order. U is
+//     four pages per streaming warp (more when the workload is huge); the
+//     sequences holding the last eighth of the pages use U / 2, so the tasks
+//     handed out last are short and the SMs run out of work together.
+//   * A persistent grid of one CTA per SM: CTA c starts on task c, then takes
+//     tasks from an atomic counter, so SMs that stream slower take fewer (the
+//     last failing grab resets the counter for the next call).
+//   * Inside a CTA, warp roles: W streaming warps, a feeder, a merger and two
+//     finishers, talking through shared memory only (bounded spins, no
+//     CTA-wide barrier):
+//       - the feeder keeps one task staged (grabbed, located, its query row
+//         and block ids loaded) and publishes it in a queue when the streaming
+//         warps are about to need it: an entry (item, pages, position in the
+//         CTA's page stream), the query row in fp32 and the block ids in a
+//         ring. Near the end of the pool it grabs only when needed.
+//       - streaming warps claim pages of the CTA's page stream one at a time
+//         (a shared counter), so every warp stays busy whatever the task
+//         sizes. A claimed page's K and V arrive by 1-D bulk copies
+//         (cp.async.bulk, the TMA engine; L2 evict-first) into the warp's own
+//         ring of stages, completing on one mbarrier per stage. The warp
+//         computes the page's (m, l, acc) and deposits it in the page's slot
+//         of a 32-slot ring.
+//       - the merger folds the page states of each task in page order, then
+//         writes the output row, or hands a split task's state on.
+//       - the finishers write a split task's partial (m, l, acc) to the
+//         workspace and take the item's ticket; the item's last task merges
+//         all of its partials, in task order, into the output row.
+//   * Q.K^T: lane = key, reading the dim-pair-major K page with conflict-free
+//     32-bit shared loads (a 16-key page: half-warps split the K rows) against
+//     the fp32 query as broadcast loads; P.V: lanes own 4 dims of a V row.
 //   * Masked keys never reach P.V (the loop stops at the last valid key), so
 //     NaN in unused slots of a page cannot leak (`paged_attn.mojo:686-687`).
+//   * A one-token append through the page table is fused: the warp that
+//     streams the new token's page patches the token into shared memory after
+//     the copy lands and writes it to the cache (it is that page's only reader
+//     in the call), so no second launch is needed.
 #pragma once
 
 #include "common.cuh"
 
 namespace ca {
 
-constexpr int kDecodeMaxChunkTokens = 128;  // keys per chunk: 4 steps of 32
-constexpr int kKSlotPadBytes = 64;          // K page slot padding: 16 banks
+constexpr int kDecodeMaxPage = 128;               // tokens per page this kernel stages
+constexpr int kKSlotPadBytes = 64;                // K page slot padding: 16 banks
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s per bounded wait
+constexpr int kDecodeMaxWarps = 10;               // streaming warps per CTA (plus a merger and a feeder)
+constexpr int kDecodeQueue = 8;                   // task queue entries per CTA
+constexpr int kDecodeAhead = 12;                  // published pages a CTA keeps unclaimed
+constexpr int kDecodeFinish = 4;                  // split tasks in flight from the merger to the finishers
+constexpr int kDecodeFinishers = 2;               // finisher warps (entry f goes to finisher f % 2)
+constexpr int kDecodePageSlots = 32;              // page states in flight to the merger
+constexpr int kDecodeBlkRing = 512;               // staged block ids per CTA (a ring over the page stream)
+constexpr int kDecodeBlkTask = 256;               // tasks up to this many pages stage their block ids
 
 struct DecodeParams {
   const void* q;
@@ -45,7 +75,10 @@ struct DecodeParams {
   const void* vc;
   long long num_blocks;
   const int* lens;
-  int extra;  // 1: the call appended a token at lens[i]
+  int extra;            // 1: the call appends a token at lens[i] (fused)
+  const void* k_new;    // the appended token's K/V rows (extra == 1)
+  const void* v_new;
+  long long kv_stride;  // elements between sequences of k_new/v_new
   const int* page_table;
   long long pt_stride;  // table width W
   void* out;
@@ -53,33 +86,24 @@ struct DecodeParams {
   int B, H, page;
   float c;  // softmax_scale * log2(e)
   // plan (host)
-  int cp;           // pages per chunk
-  int stages;       // ring depth per warp
-  int warp_bytes;   // shared bytes per warp
-  int stage_bytes;  // bytes per stage
-  int kslot_bytes;  // K page bytes + padding
-  int page_bytes;   // bytes of one (block, head) page of K (equally of V)
-  int warps;        // worker warps per CTA
-  float* partial;   // [2 * workers][E + 2]
-  int* tickets;     // [B * H], zero between calls
-  int* status;      // CA_STATUS_* bits
+  int stages;          // ring depth per warp
+  int warp_bytes;      // shared bytes per streaming warp (ring, probabilities, barriers)
+  int stage_bytes;     // one K page slot + one V page
+  int kslot_bytes;     // K page bytes + padding
+  int page_bytes;      // bytes of one (block, head) page of K (equally of V)
+  int warps;           // streaming warps per CTA (two more warps serve them)
+  int pages_per_warp;  // task size U = warps * pages_per_warp (or more)
+  int ahead;           // published pages the feeder keeps unclaimed
+  int tail_div;        // the last tasks are 1 / tail_div the size of the others
+  int task_cap;        // tasks of split items number at most 2 * task_cap
+  float* partial;      // [2 * task_cap + 2][E + 2]
+  int* tickets;        // [B * H], zero between calls
+  int* status;         // CA_STATUS_* bits
+  int* counter;        // tasks handed out, zero between calls
 };
 
-struct ChunkHdr {
-  int i, h;     // sequence, head
-  int npg;      // pages in this chunk
-  int ntok;     // valid keys in this chunk
-  int flags;    // kFirst | kLast | kWhole | kEnd
-  int np;       // pages of the item (sequence i)
-  int slot;     // partial slot of this piece (pieces only)
-  int pad;
-  long long ux;  // first unit of the item
-};
-constexpr int kFirst = 1, kLast = 2, kWhole = 4, kEnd = 8;
-
-// Pages of sequence i's attended length (clamped, and flagged, when the
-// length exceeds the page table: the reference declines that call,
-// `_C.mojo:148-153`).
+// Attended length of sequence i (clamped, and flagged, when it exceeds the
+// page table: the reference declines that call, `_C.mojo:148-153`) and its pages.
 __device__ __forceinline__ int seq_pages(const DecodeParams& p, int i, int* len_out) {
   long long L = (long long)__ldg(p.lens + i) + p.extra;
   const long long cap = p.pt_stride * (long long)p.page;
@@ -92,12 +116,74 @@ __device__ __forceinline__ int seq_pages(const DecodeParams& p, int i, int* len_
   return (int)((L + p.page - 1) / p.page);
 }
 
-// Worker k's first unit: floor(k * P / G).
-__device__ __forceinline__ long long range_start(long long k, long long P, long long G) { return (k * P) / G; }
-// The worker whose range holds unit u: the largest k with floor(kP/G) <= u.
-__device__ __forceinline__ long long worker_of(long long u, long long P, long long G) {
-  return ((u + 1) * G - 1) / P;
-}
+// Tasks of an item of np pages.
+__device__ __forceinline__ int item_tasks(int np, int U) { return np <= U ? 1 : (np + U - 1) / U; }
+
+// Task sizes: items of sequences before icut are cut into tasks of at most
+// Ub pages, the rest (the last sequences, about an eighth of the pages: the
+// tasks handed out last) into tasks of at most Us pages, so that the
+// CTAs run out of work at nearly the same time.
+struct TaskPlan {
+  int Ub, Us, icut;
+  __device__ __forceinline__ int size(int i) const { return i < icut ? Ub : Us; }
+};
+
+// Where a task lives.
+struct Task {
+  int i, h;        // item
+  int np, len;     // pages and attended length of sequence i
+  int raw;         // cache_seqlens[i] as given
+  int ntask, j;    // tasks of the item, and which one this is
+  int pg0, pg1;    // pages [pg0, pg1)
+  long long slot;  // partial slot of this task (items with ntask > 1)
+};
+
+// Maps task ids, which only grow per walker, to tasks with a forward scan over
+// the sequences, 32 at a time (warp-collective).
+struct TaskWalk {
+  int ci0 = 0;          // first of the 32 sequences the scan starts at
+  long long tbase = 0;  // first task id of sequence ci0
+  long long sbase = 0;  // first partial slot of sequence ci0
+  __device__ __forceinline__ Task locate(const DecodeParams& p, const TaskPlan& plan, long long tid, int lane) {
+    Task t;
+    for (int i0 = ci0;; i0 += 32) {
+      const int i = i0 + lane;
+      int L = 0, np = 0, nt = 0, raw = 0;
+      if (i < p.B) {
+        raw = __ldg(p.lens + i);
+        np = seq_pages(p, i, &L);
+        nt = item_tasks(np, plan.size(i));
+      }
+      const long long tk = (long long)nt * p.H, sl = nt > 1 ? tk : 0;
+      const long long tincl = warp_scan_ll(tk, lane) + tbase;
+      const long long sincl = warp_scan_ll(sl, lane) + sbase;
+      const unsigned hit = __ballot_sync(0xffffffffu, i < p.B && tincl > tid);
+      if (hit) {
+        const int src = __ffs(hit) - 1;
+        t.i = i0 + src;
+        t.np = __shfl_sync(0xffffffffu, np, src);
+        t.len = __shfl_sync(0xffffffffu, L, src);
+        t.raw = __shfl_sync(0xffffffffu, raw, src);
+        t.ntask = __shfl_sync(0xffffffffu, nt, src);
+        const long long t0 = __shfl_sync(0xffffffffu, tincl - tk, src);
+        const long long s0 = __shfl_sync(0xffffffffu, sincl - sl, src);
+        const int off = (int)(tid - t0);
+        t.h = off / t.ntask;
+        t.j = off - t.h * t.ntask;
+        t.pg0 = (int)((long long)t.j * t.np / t.ntask);  // even split of the item's pages
+        t.pg1 = (int)((long long)(t.j + 1) * t.np / t.ntask);
+        t.slot = t.ntask > 1 ? s0 + off : -1;
+        // keep the scan at this group of 32; the next task is here or later
+        tbase = __shfl_sync(0xffffffffu, tincl - tk, 0);
+        sbase = __shfl_sync(0xffffffffu, sincl - sl, 0);
+        ci0 = i0;
+        return t;
+      }
+      tbase = __shfl_sync(0xffffffffu, tincl, 31);
+      sbase = __shfl_sync(0xffffffffu, sincl, 31);
+    }
+  }
+};
 
 template <typename T, int E>
 struct DecodeTile {
@@ -107,344 +193,762 @@ struct DecodeTile {
   static constexpr int kKeysPerStep = 32 / kLanesPerKey;
 };
 
+// Bounded wait that also returns at once when this CTA already gave up.
+__device__ __forceinline__ bool decode_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 255u) == 0 && (*abort || global_timer_ns() - t0 > kWaitLimitNs)) return false;
+  }
+}
+
+// One published task in a CTA's queue (written by the feeder warp; read by
+// the streaming warps and the merger until the merger is done with it).
+struct QueueEntry {
+  int id;          // task id, -1: no more tasks
+  int i, h;        // item
+  int ntask, j;    // tasks of the item, and which one this is
+  int pg0;         // first page of the task
+  int n;           // pages of the task
+  int start;       // the task's first page in the CTA's page stream
+  int len;         // attended length of sequence i
+  int apg;         // page holding the appended token, -1: none in this task
+  int staged;      // 1: its block ids are in the CTA's block-id ring
+  long long slot;  // partial slot (ntask > 1)
+};
+
+// A split task's merged state on its way from the merger to the finisher.
+struct FinishEntry {
+  int i, h, ntask, j;  // i < 0: no more
+  long long slot;
+  float m, l;
+};
+
+// CTA area after the streaming warps' rings (byte offsets; the host sizes it
+// with decode_cta_bytes).
+constexpr int kCtaInts = 0;                       // counters and flags, see the kernel
+constexpr int kCtaEntries = 4 * 128;              // QueueEntry[kDecodeQueue]
+constexpr int kCtaFinish = kCtaEntries + (int)sizeof(QueueEntry) * kDecodeQueue;  // FinishEntry[kDecodeFinish]
+constexpr int kCtaRows = kCtaFinish + (int)sizeof(FinishEntry) * kDecodeFinish;   // float rows
+__host__ __device__ constexpr int decode_cta_bytes(int E, int warps) {
+  // query rows [QD][E], finisher accumulators [FQ][E], page states [R][E + 4], block ids [RB]
+  return kCtaRows + kDecodeQueue * E * 4 + kDecodeFinish * E * 4 + kDecodePageSlots * (E + 4) * 4 +
+         kDecodeBlkRing * 4 + 0 * warps;
+}
+// Per streaming warp, behind its ring: probabilities, stage tags (task
+// position, page, stream index; 16-byte aligned), stage barriers.
+__host__ __device__ constexpr int decode_warp_bytes(int stages, int stage_bytes) {
+  return (stages * stage_bytes + kDecodeMaxPage * 4 + stages * 8 + stages * 16 + 127) / 128 * 128;
+}
+
+// Spins until `ok()` (bounded; false on timeout or abort).
+template <typename F>
+__device__ __forceinline__ bool spin_until(F ok, volatile int* abort) {
+  if (ok()) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (ok()) return true;
+    if ((it & 63u) == 0 && (*abort || global_timer_ns() - t0 > kWaitLimitNs)) return false;
+    __nanosleep(32);
+  }
+}
+
 template <typename T, int E>
-__global__ void __launch_bounds__(256, 1) decode_kernel(const __grid_constant__ DecodeParams p) {
+__global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers), 1) decode_kernel(const __grid_constant__ DecodeParams p) {
   using Tile = DecodeTile<T, E>;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  const long long Gall = (long long)gridDim.x * p.warps;
-  const long long k = (long long)blockIdx.x * p.warps + warp;
+  const int w = threadIdx.x >> 5;
+  const int W = p.warps;  // streaming warps; then the merger, the feeder and the finishers
+  constexpr int QD = kDecodeQueue, FQ = kDecodeFinish, R = kDecodePageSlots;
 
-  // ---- this warp's shared memory
-  uint8_t* wbase = smem_raw + (size_t)warp * p.warp_bytes;
-  float* sQ = reinterpret_cast<float*>(wbase + (size_t)p.stages * p.stage_bytes);
-  float* sP = sQ + E;
-  ChunkHdr* sHdr = reinterpret_cast<ChunkHdr*>(sP + kDecodeMaxChunkTokens);
-  uint64_t* sBar = reinterpret_cast<uint64_t*>(sHdr + p.stages);
+  // ---- CTA area
+  uint8_t* cta = smem_raw + (size_t)W * p.warp_bytes;
+  volatile int* sInts = reinterpret_cast<volatile int*>(cta + kCtaInts);
+  volatile int* sSeq = sInts;                  // [QD] queue entry r holds task position sSeq[r] (-1: being written)
+  volatile int* sFlag = sInts + QD;            // [R] page slot r holds stream page sFlag[r]
+  volatile int* sFin = sInts + QD + R;         // [FQ] finisher entry r holds split task sFin[r]
+  volatile int* sMerged = sFin + FQ;           // tasks merged (their queue entries are free)
+  volatile int* sMergedPages = sFin + FQ + 1;  // stream pages merged (their slots are free)
+  volatile int* sAbort = sFin + FQ + 2;
+  int* sNext = const_cast<int*>(sFin + FQ + 3);  // stream pages claimed
+  volatile int* sFinAck = sFin + FQ + 4;       // [FQ] finisher entry r was last taken for split task sFinAck[r]
+  volatile QueueEntry* sQe = reinterpret_cast<volatile QueueEntry*>(cta + kCtaEntries);
+  volatile FinishEntry* sFe = reinterpret_cast<volatile FinishEntry*>(cta + kCtaFinish);
+  float* sRows = reinterpret_cast<float*>(cta + kCtaRows);  // [QD][E]
+  float* sFinO = sRows + QD * E;                              // [FQ][E]
+  float* sPage = sFinO + FQ * E;                              // [R][E + 4]: acc[E], m, l
+  int* sBlk = reinterpret_cast<int*>(sPage + R * (E + 4));   // [RB]: block id of stream page g at g % RB
 
-  // ---- plan: total units P, then this worker's range [a, b)
-  long long P = 0;
+  // ---- plan: task sizes and the number of tasks (every warp alike)
+  long long NP = 0, NT = 0;
   for (int i0 = 0; i0 < p.B; i0 += 32) {
     const int i = i0 + lane;
     if (i < p.B) {
       int L;
-      P += (long long)(seq_pages(p, i, &L) + 1) * p.H;
+      NP += seq_pages(p, i, &L);
     }
   }
-  P = warp_sum_ll(P);
-  // With fewer units than warps only the first P warps work, so that every
-  // worker range is non-empty (the merge counts one piece per worker).
-  const long long G = min(Gall, P);
-  if (k >= G) return;
-  const long long a = range_start(k, P, G), b = range_start(k + 1, P, G);
-
-  // the item holding unit a
-  int pi = 0, pnp = 0, plen = 0, ph = 0;
-  long long pU = 0;  // first unit of sequence pi
-  {
+  NP = warp_sum_ll(NP) * p.H;
+  TaskPlan plan;
+  plan.Ub = W * p.pages_per_warp;
+  if (NP > (long long)p.task_cap * plan.Ub) plan.Ub = (int)((NP + p.task_cap - 1) / p.task_cap);
+  plan.Us = max(W, plan.Ub / p.tail_div);
+  plan.icut = p.B;
+  if (plan.Us < plan.Ub) {
+    // the first sequence from which on at most an eighth of the pages remain
+    const long long need = NP - NP / 8;
     long long base = 0;
-    for (int i0 = 0;; i0 += 32) {
+    for (int i0 = 0; i0 < p.B && plan.icut == p.B; i0 += 32) {
       const int i = i0 + lane;
-      int L = 0, np = 0;
-      long long units = 0;
-      if (i < p.B) {
-        np = seq_pages(p, i, &L);
-        units = (long long)(np + 1) * p.H;
-      }
-      const long long incl = warp_scan_ll(units, lane) + base;
-      const unsigned hit = __ballot_sync(0xffffffffu, i < p.B && incl > a);
+      int L = 0;
+      const long long pg = i < p.B ? (long long)seq_pages(p, i, &L) * p.H : 0;
+      const long long before = warp_scan_ll(pg, lane) - pg + base;
+      const unsigned hit = __ballot_sync(0xffffffffu, i < p.B && before >= need);
       if (hit) {
         const int src = __ffs(hit) - 1;
-        pi = i0 + src;
-        pnp = __shfl_sync(0xffffffffu, np, src);
-        plen = __shfl_sync(0xffffffffu, L, src);
-        pU = __shfl_sync(0xffffffffu, incl - units, src);
+        plan.icut = i0 + src;
+        base = __shfl_sync(0xffffffffu, before, src);
+      } else {
+        base = __shfl_sync(0xffffffffu, before + pg, 31);
+      }
+    }
+    const long long tail = NP - base;  // pages of the small tasks (base: pages before icut)
+    // only when every CTA gets a small task or more, and the split tasks keep
+    // within the partial slots (at most 2 np / U slots per split item)
+    if (plan.icut == p.B || tail < (long long)gridDim.x * plan.Us ||
+        2 * tail / plan.Us + 2 * NP / plan.Ub > 2LL * p.task_cap)
+      plan.icut = p.B;
+  }
+  for (int i0 = 0; i0 < p.B; i0 += 32) {
+    const int i = i0 + lane;
+    if (i < p.B) {
+      int L;
+      NT += item_tasks(seq_pages(p, i, &L), plan.size(i));
+    }
+  }
+  NT = warp_sum_ll(NT) * p.H;
+
+  uint8_t* wbase = smem_raw + (size_t)w * p.warp_bytes;
+  float* sP = reinterpret_cast<float*>(wbase + (size_t)p.stages * p.stage_bytes);
+  int4* sTag = reinterpret_cast<int4*>(sP + kDecodeMaxPage);  // per stage: task position, page, stream page
+  uint64_t* sBar = reinterpret_cast<uint64_t*>(sTag + p.stages);
+  if (threadIdx.x < 128)
+    sInts[threadIdx.x] = (threadIdx.x < QD + R + FQ || (threadIdx.x >= QD + R + FQ + 4 && threadIdx.x < QD + R + 2 * FQ + 4)) ? -1 : 0;
+  if (w < W && lane == 0)
+    for (int s = 0; s < p.stages; ++s) mbar_init(&sBar[s], 1);
+  fence_barrier_init();
+  __syncthreads();
+
+  const int dg = lane % Tile::kLanesPerKey;  // P.V and merges: dims 4*dg .. 4*dg+3
+  const int tg = lane / Tile::kLanesPerKey;  // P.V: keys tg, tg + kKeysPerStep, ...
+
+  if (w == W + 1) {
+    // ================================================================= feeder
+    // Keeps one task staged (grabbed, located, its query row in registers)
+    // and publishes it while fewer than p.ahead published pages are unclaimed
+    // and a queue entry is free (merged); then stages the next, so the grab's
+    // and the loads' latency overlap the wait. Every CTA makes exactly one
+    // failing grab; the last one overall resets the counter for the next call.
+    TaskWalk walk;
+    const T* qbase = static_cast<const T*>(p.q);
+    constexpr int QR = (E + 31) / 32;
+    constexpr int BR = kDecodeBlkTask / 32;
+    int sid = -1, sapg = -1;  // staged task id (-1: the failing grab), appended page
+    Task st;
+    T qraw[QR];
+    int sblk[BR];  // the task's block ids (tasks of at most kDecodeBlkTask pages)
+    // Task c < gridDim.x is CTA c's first task; the others come from the
+    // counter (id = gridDim.x + counter). Each CTA with a first task makes
+    // exactly one failing grab, so the last grab overall reads NT - 1.
+    bool first = true;
+    auto stage_next = [&]() {
+      int id = -1;
+      if (first) {
+        first = false;
+        if (blockIdx.x < NT) id = blockIdx.x;
+      } else {
+        if (lane == 0) {
+          const long long tt = atomicAdd(p.counter, 1);
+          if (gridDim.x + tt < NT) id = (int)(gridDim.x + tt);
+          if (tt == NT - 1) *p.counter = 0;
+        }
+        id = __shfl_sync(0xffffffffu, id, 0);
+      }
+      sid = id;
+      if (sid < 0) return;
+      st = walk.locate(p, plan, sid, lane);
+      const T* qr = qbase + (long long)st.i * p.q_stride + (long long)st.h * E;
+#pragma unroll
+      for (int k = 0; k < QR; ++k)
+        if (lane + 32 * k < E) qraw[k] = qr[lane + 32 * k];
+      sapg = -1;
+      if (p.extra && st.len == st.raw + 1) {
+        const int apg = (st.len - 1) / p.page;
+        if (apg >= st.pg0 && apg < st.pg1) sapg = apg;
+      }
+      const int n = st.pg1 - st.pg0;
+      if (n <= kDecodeBlkTask) {
+        const int* row = p.page_table + (long long)st.i * p.pt_stride + st.pg0;
+#pragma unroll
+        for (int k = 0; k < BR; ++k) {
+          const int idx = lane + 32 * k;
+          int blk = 0;
+          if (idx < n) {
+            blk = __ldg(row + idx);
+            if (blk < 0 || blk >= p.num_blocks) {
+              atomicOr(p.status, CA_STATUS_TABLE);
+              blk = 0;
+            }
+          }
+          sblk[k] = blk;
+        }
+      }
+    };
+    stage_next();
+    bool staged = true;
+    int published = 0;  // pages of the tasks published so far
+    auto give_up = [&]() {
+      if (lane == 0) {
+        atomicOr(p.status, CA_STATUS_TIMEOUT);
+        *sAbort = 1;
+        while (!staged || sid >= 0) {  // still make the failing grab
+          const long long tt = atomicAdd(p.counter, 1);
+          if (tt == NT - 1) *p.counter = 0;
+          if (gridDim.x + tt >= NT) break;
+        }
+      }
+    };
+    for (int qg = 0;; ++qg) {
+      if (!staged) {
+        // near the end of the pool: grab only once this CTA needs the task
+        if (!spin_until([&] { return qg - *sMerged < QD && published - *(volatile int*)sNext < p.ahead; }, sAbort)) {
+          give_up();
+          break;
+        }
+        stage_next();
+        staged = true;
+      }
+      const int sn = sid >= 0 ? st.pg1 - st.pg0 : 0;
+      const bool fast = sn <= kDecodeBlkTask;
+      if (!spin_until([&] {
+            return qg - *sMerged < QD && published - *(volatile int*)sNext < p.ahead &&
+                   (!fast || published + sn - *sMergedPages <= kDecodeBlkRing);
+          }, sAbort)) {
+        give_up();
         break;
       }
-      base = __shfl_sync(0xffffffffu, incl, 31);
+      const int r = qg % QD;
+      volatile QueueEntry* e = sQe + r;
+      if (lane == 0) sSeq[r] = -1;  // being rewritten
+      __syncwarp();
+      __threadfence_block();
+      if (sid >= 0) {
+        float* row = sRows + r * E;
+#pragma unroll
+        for (int k = 0; k < QR; ++k)
+          if (lane + 32 * k < E) row[lane + 32 * k] = to_f32(qraw[k]);
+        if (fast) {
+#pragma unroll
+          for (int k = 0; k < BR; ++k)
+            if (lane + 32 * k < sn) sBlk[(published + lane + 32 * k) % kDecodeBlkRing] = sblk[k];
+        }
+        if (lane == 0) {
+          e->id = sid;
+          e->i = st.i;
+          e->h = st.h;
+          e->ntask = st.ntask;
+          e->j = st.j;
+          e->pg0 = st.pg0;
+          e->n = st.pg1 - st.pg0;
+          e->start = published;
+          e->len = st.len;
+          e->apg = sapg;
+          e->staged = fast ? 1 : 0;
+          e->slot = st.slot;
+        }
+        published += st.pg1 - st.pg0;
+      } else if (lane == 0) {
+        e->id = -1;
+        e->n = 0;
+        e->start = published;
+      }
+      __syncwarp();
+      __threadfence_block();
+      if (lane == 0) sSeq[r] = qg;
+      if (sid < 0) break;
+      // while more than two tasks per CTA remain, grab the next one at once
+      // (its latency hides behind the wait); near the end, only when needed
+      staged = NT - sid > 2LL * gridDim.x;
+      if (staged) stage_next();
     }
-    ph = (int)((a - pU) / (pnp + 1));
+    return;
   }
-  long long pUX = pU + (long long)ph * (pnp + 1);  // first unit of item (pi, ph)
-  long long u = a;                                 // next unit to produce
-  long long piece_start = a;
 
-  if (lane == 0) {
-    for (int s = 0; s < p.stages; ++s) mbar_init(&sBar[s], 1);
-    fence_barrier_init();
+  if (w == W) {
+    // ================================================================= merger
+    // Combines the page states of each task in page order (so the result
+    // does not depend on which warp streamed which page), frees the page
+    // slots and the queue entry, then writes the output row, or hands a split
+    // task's state to the finisher.
+    T* obase = static_cast<T*>(p.out);
+    int nf = 0;  // split tasks handed over
+    bool ok = true;
+    for (int q = 0; ok; ++q) {
+      const int r = q % QD;
+      if (!spin_until([&] { return sSeq[r] == q; }, sAbort)) {
+        ok = false;
+        break;
+      }
+      __threadfence_block();
+      const int id = sQe[r].id;
+      if (id < 0) break;
+      const int ei = sQe[r].i, eh = sQe[r].h, entask = sQe[r].ntask, ej = sQe[r].j, en = sQe[r].n,
+                est = sQe[r].start;
+      const long long eslot = sQe[r].slot;
+      float M = -INFINITY, L = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int gg = est; gg < est + en; ++gg) {
+        const int ps = gg % R;
+        if (!spin_until([&] { return sFlag[ps] == gg; }, sAbort)) {
+          ok = false;
+          break;
+        }
+        __threadfence_block();
+        const float* st = sPage + ps * (E + 4);
+        const float mp = st[E], lp = st[E + 1];
+        float a[4];
+        if (lane < Tile::kLanesPerKey) {
+          const float4 v4 = *reinterpret_cast<const float4*>(st + dg * 4);
+          a[0] = v4.x, a[1] = v4.y, a[2] = v4.z, a[3] = v4.w;
+        }
+        __syncwarp();
+        if (lane == 0) *sMergedPages = gg + 1;  // slot ps is free
+        const float Mn = fmaxf(M, mp);
+        const float so = exp2_approx(M - Mn), sp = exp2_approx(mp - Mn);  // M = -inf: 0
+        L = fmaf(L, so, lp * sp);
+        if (lane < Tile::kLanesPerKey) {
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) o[cc] = fmaf(o[cc], so, a[cc] * sp);
+        }
+        M = Mn;
+      }
+      if (!ok) break;
+      __syncwarp();
+      if (lane == 0) *sMerged = q + 1;  // the queue entry is free
+      if (entask == 1) {
+        T* orow = obase + (long long)ei * p.out_stride + (long long)eh * E;
+        if (lane < Tile::kLanesPerKey) {
+          const float inv = L > 0.f ? 1.f / L : 0.f;
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) orow[dg * 4 + cc] = from_f32<T>(L > 0.f ? o[cc] * inv : 0.f);
+        }
+        continue;
+      }
+      // ---- a split task: to the finisher
+      const int fr = nf % FQ;
+      if (!spin_until([&] { return nf < FQ || sFinAck[fr] == nf - FQ; }, sAbort)) {
+        ok = false;
+        break;
+      }
+      if (lane < Tile::kLanesPerKey) *reinterpret_cast<float4*>(sFinO + fr * E + dg * 4) = make_float4(o[0], o[1], o[2], o[3]);
+      if (lane == 0) {
+        sFe[fr].i = ei;
+        sFe[fr].h = eh;
+        sFe[fr].ntask = entask;
+        sFe[fr].j = ej;
+        sFe[fr].slot = eslot;
+        sFe[fr].m = M;
+        sFe[fr].l = L;
+      }
+      __syncwarp();
+      __threadfence_block();
+      if (lane == 0) sFin[fr] = nf;
+      ++nf;
+    }
+    if (!ok && lane == 0) {
+      atomicOr(p.status, CA_STATUS_TIMEOUT);
+      *sAbort = 1;
+    }
+    // an end marker for each finisher (they also stop on abort)
+    for (int k = 0; k < kDecodeFinishers; ++k, ++nf) {
+      const int fr = nf % FQ;
+      if (!spin_until([&] { return nf < FQ || sFinAck[fr] == nf - FQ; }, sAbort)) break;
+      if (lane == 0) {
+        sFe[fr].i = -1;
+        __threadfence_block();
+        sFin[fr] = nf;
+      }
+    }
+    return;
   }
-  __syncwarp();
+
+  if (w >= W + 2) {
+    // ============================================================== finishers
+    // Split tasks: writes the task's partial (m, l, acc), takes the item's
+    // ticket, and the item's last task to finish merges all of its partials
+    // (in task order) into the output row. Finisher k takes the split tasks
+    // k, k + kDecodeFinishers, ... so that their global round trips overlap.
+    T* obase = static_cast<T*>(p.out);
+    for (int f = w - (W + 2);; f += kDecodeFinishers) {
+      const int fr = f % FQ;
+      if (!spin_until([&] { return sFin[fr] == f; }, sAbort)) break;
+      __threadfence_block();
+      const int ei = sFe[fr].i;
+      if (ei < 0) break;
+      const int eh = sFe[fr].h, entask = sFe[fr].ntask, ej = sFe[fr].j;
+      const long long eslot = sFe[fr].slot;
+      const float M = sFe[fr].m, L = sFe[fr].l;
+      float o[4] = {0.f, 0.f, 0.f, 0.f};
+      if (lane < Tile::kLanesPerKey) {
+        const float4 v4 = *reinterpret_cast<const float4*>(sFinO + fr * E + dg * 4);
+        o[0] = v4.x, o[1] = v4.y, o[2] = v4.z, o[3] = v4.w;
+      }
+      __syncwarp();
+      if (lane == 0) sFinAck[fr] = f;
+      float* slot = p.partial + eslot * (E + 2);
+      if (lane < Tile::kLanesPerKey) {
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) slot[2 + dg * 4 + cc] = o[cc];
+      }
+      if (lane == 0) {
+        slot[0] = M;
+        slot[1] = L;
+      }
+      fence_acq_rel_gpu();  // the partial before the ticket (release)
+      __syncwarp();
+      int ticket = 0;
+      int* tk = p.tickets + (long long)ei * p.H + eh;
+      if (lane == 0) ticket = atomicAdd(tk, 1);
+      ticket = __shfl_sync(0xffffffffu, ticket, 0);
+      if (ticket != entask - 1) continue;
+      fence_acq_rel_gpu();  // the other tasks' partials after their tickets (acquire)
+      const float* first = p.partial + (eslot - ej) * (E + 2);
+      float MM = -INFINITY;
+      for (int jj = lane; jj < entask; jj += 32) MM = fmaxf(MM, __ldcg(first + (long long)jj * (E + 2)));
+      MM = warp_max(MM);
+      float LL = 0.f, oo[4] = {0.f, 0.f, 0.f, 0.f};
+      if (MM != -INFINITY) {
+#pragma unroll 4
+        for (int jj = 0; jj < entask; ++jj) {  // task order, every lane alike
+          const float* ps = first + (long long)jj * (E + 2);
+          const float wt = exp2_approx(__ldcg(ps) - MM);
+          LL = fmaf(__ldcg(ps + 1), wt, LL);
+          if (lane < Tile::kLanesPerKey) {
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) oo[cc] = fmaf(__ldcg(ps + 2 + dg * 4 + cc), wt, oo[cc]);
+          }
+        }
+      }
+      T* orow = obase + (long long)ei * p.out_stride + (long long)eh * E;
+      if (lane < Tile::kLanesPerKey) {
+        const float inv = LL > 0.f ? 1.f / LL : 0.f;
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) orow[dg * 4 + cc] = from_f32<T>(LL > 0.f ? oo[cc] * inv : 0.f);
+      }
+      if (lane == 0) *tk = 0;  // ready for the next call
+    }
+    return;
+  }
+
+  // ================================================================ streaming
   const uint64_t policy = l2_evict_first_policy();
   const char* kc = static_cast<const char*>(p.kc);
   const char* vc = static_cast<const char*>(p.vc);
+  const int vrow_words = E * (int)sizeof(T) / 4;
 
-  // ---- producer: fill stage s with the next chunk of this worker's range
-  auto produce = [&](int s) {
-    ChunkHdr hdr;
-    hdr.pad = 0;
-    uint8_t* stage = wbase + (size_t)s * p.stage_bytes;
-    if (u >= b) {
+  // ---- producer: claims the CTA's next page (a shared counter over the pages
+  // of the published tasks, in queue order) whenever the ring has room, and
+  // issues its copies. A claim past the published pages stays pending until
+  // its task is published; a claim past the end marker ends the producer.
+  int g = -1;                 // pending claim (-1: none)
+  bool pdone = false;         // the end marker was reached
+  int cq = 0;                 // queue position the walk is at
+  int c_start = 0, c_n = -1;  // its pages in the stream (c_n < 0: not read)
+  int c_i = 0, c_h = 0, c_pg0 = 0, c_staged = 0;
+  unsigned pidx = 0, cidx = 0;  // pages produced / consumed
+  auto produce = [&]() {
+    while (!pdone && pidx - cidx < (unsigned)p.stages) {
+      if (g < 0) {
+        int gg = 0;
+        if (lane == 0) gg = atomicAdd(sNext, 1);
+        g = __shfl_sync(0xffffffffu, gg, 0);
+      }
+      // find the task of page g (tasks only move forward)
+      for (;;) {
+        if (c_n < 0) {
+          if (*sMerged > cq) {  // merged already: none of its pages is g
+            ++cq;
+            continue;
+          }
+          const int r = cq % QD;
+          if (sSeq[r] != cq) return;  // not published yet: keep the claim pending
+          __threadfence_block();
+          const int id = sQe[r].id, st = sQe[r].start, n = sQe[r].n;
+          const int ii = sQe[r].i, hh = sQe[r].h, pg0 = sQe[r].pg0, stg = sQe[r].staged;
+          __threadfence_block();
+          if (sSeq[r] != cq) continue;  // rewritten while read: look again
+          if (id < 0) {
+            pdone = true;
+            return;
+          }
+          c_start = st;
+          c_n = n;
+          c_i = ii;
+          c_h = hh;
+          c_pg0 = pg0;
+          c_staged = stg;
+        }
+        if (g < c_start + c_n) break;
+        ++cq;
+        c_n = -1;
+      }
+      const int s = (int)(pidx % (unsigned)p.stages);
+      const int pg = c_pg0 + (g - c_start);
+      uint8_t* stage = wbase + (size_t)s * p.stage_bytes;
       if (lane == 0) {
-        hdr.flags = kEnd;
-        hdr.i = hdr.h = hdr.npg = hdr.ntok = hdr.np = hdr.slot = 0;
-        hdr.ux = 0;
-        sHdr[s] = hdr;
-        mbar_arrive_expect_tx(&sBar[s], 0);
+        sTag[s] = make_int4(cq, pg, g, 0);
+        int blk;
+        if (c_staged) {
+          blk = sBlk[g % kDecodeBlkRing];  // checked by the feeder
+        } else {
+          blk = __ldg(p.page_table + (long long)c_i * p.pt_stride + pg);
+          if (blk < 0 || blk >= p.num_blocks) {
+            atomicOr(p.status, CA_STATUS_TABLE);
+            blk = 0;
+          }
+        }
+        const long long off = ((long long)blk * p.H + c_h) * (long long)p.page_bytes;
+        mbar_arrive_expect_tx(&sBar[s], (uint32_t)(2 * p.page_bytes));
+        fence_proxy_async_smem();
+        bulk_g2s(stage, kc + off, (uint32_t)p.page_bytes, &sBar[s], policy);
+        bulk_g2s(stage + p.kslot_bytes, vc + off, (uint32_t)p.page_bytes, &sBar[s], policy);
       }
-      return;
+      __syncwarp();
+      ++pidx;
+      g = -1;
     }
-    if (u == pUX + pnp + 1) {  // the item is done: next head, then next sequence
-      pUX = u;
-      piece_start = u;
-      if (++ph == p.H) {
-        ph = 0;
-        ++pi;
-        pnp = seq_pages(p, pi, &plen);
-      }
-    }
-    const int pg = (int)(u - pUX);
-    int n = 0;
-    int flags = (u == piece_start) ? kFirst : 0;
-    if (pg < pnp) {
-      n = min(p.cp, pnp - pg);
-      n = (int)min((long long)n, b - u);
-      u += n;
-      if (u == pUX + pnp && u < b) u += 1;  // the item's fixed-cost unit joins this piece
-    } else {
-      u += 1;  // only the fixed-cost unit
-    }
-    const bool last = (u == pUX + pnp + 1) || (u == b);
-    if (last) flags |= kLast;
-    if (last && piece_start == pUX && u == pUX + pnp + 1) flags |= kWhole;
-    const int tok0 = pg * p.page;
-    const int ntok = n ? min(plen, (pg + n) * p.page) - tok0 : 0;
-    if (lane == 0) {
-      hdr.i = pi;
-      hdr.h = ph;
-      hdr.npg = n;
-      hdr.ntok = ntok;
-      hdr.flags = flags;
-      hdr.np = pnp;
-      hdr.slot = (int)(2 * k + (piece_start == a ? 0 : 1));
-      hdr.ux = pUX;
-      sHdr[s] = hdr;
-      mbar_arrive_expect_tx(&sBar[s], (uint32_t)(2 * n * p.page_bytes));
-    }
-    __syncwarp();
-    if (lane < n) {
-      int blk = __ldg(p.page_table + (long long)pi * p.pt_stride + pg + lane);
-      if (blk < 0 || blk >= p.num_blocks) {
-        atomicOr(p.status, CA_STATUS_TABLE);
-        blk = 0;
-      }
-      const long long off = ((long long)blk * p.H + ph) * (long long)p.page_bytes;
-      fence_proxy_async_smem();
-      bulk_g2s(stage + (size_t)lane * p.kslot_bytes, kc + off, (uint32_t)p.page_bytes, &sBar[s], policy);
-      bulk_g2s(stage + (size_t)p.cp * p.kslot_bytes + (size_t)lane * p.page_bytes, vc + off,
-               (uint32_t)p.page_bytes, &sBar[s], policy);
-    }
-    if (last) piece_start = u;
   };
 
-  for (int s = 0; s < p.stages; ++s) produce(s);
-
-  // ---- consumer state
-  float m = -INFINITY, lpart = 0.f;
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  const int dg = lane % Tile::kLanesPerKey;  // P.V: dims 4*dg .. 4*dg+3
-  const int tg = lane / Tile::kLanesPerKey;  // P.V: keys tg, tg + kKeysPerStep, ...
-  const int ksw = p.kslot_bytes / 4;         // K slot stride in words
-  const int vrow_words = E * (int)sizeof(T) / 4;
-  const int vpage_words = p.page_bytes / 4;
-  const T* qbase = static_cast<const T*>(p.q);
-  T* obase = static_cast<T*>(p.out);
-
-  for (unsigned idx = 0;; ++idx) {
-    const int s = (int)(idx % (unsigned)p.stages);
-    const uint32_t parity = (idx / (unsigned)p.stages) & 1u;
-    if (!mbar_wait_bounded(&sBar[s], parity, kWaitLimitNs)) {
-      if (lane == 0) atomicOr(p.status, CA_STATUS_TIMEOUT);
-      // give the copies still in flight one more bounded chance, then leave
-      for (int r = 0; r < p.stages; ++r) {
-        const unsigned j = idx + r;
-        mbar_wait_bounded(&sBar[j % p.stages], (j / p.stages) & 1u, kWaitLimitNs);
+  // ---- consumer: each page on its own (m, l, acc), deposited in the page
+  // slot of its stream position for the merger
+  bool failed = false;    // a bounded wait gave up: stop (the other warps stop too)
+  unsigned fail_idx = 0;  // the first page not waited for
+  int cur = -1;           // task position whose fields are loaded
+  struct {
+    int i, h, len, apg;
+  } t = {0, 0, 0, -1};
+  const float* sQ = sRows;
+  for (;;) {
+    produce();
+    if (pidx == cidx) {
+      if (pdone) break;
+      if (!spin_until([&] {
+            produce();
+            return pidx != cidx || pdone;
+          }, sAbort)) {
+        failed = true;
+        fail_idx = cidx;
+        break;
       }
-      return;
+      continue;
     }
-    const ChunkHdr hdr = sHdr[s];
-    if (hdr.flags & kEnd) break;
-    const uint8_t* stage = wbase + (size_t)s * p.stage_bytes;
-
-    if (hdr.flags & kFirst) {
-      const T* qr = qbase + (long long)hdr.i * p.q_stride + (long long)hdr.h * E;
-#pragma unroll
-      for (int d = lane; d < E; d += 32) sQ[d] = to_f32(qr[d]);
-      m = -INFINITY;
-      lpart = 0.f;
-      acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
-      __syncwarp();
+    const int s = (int)(cidx % (unsigned)p.stages);
+    const int4 tag = sTag[s];
+    if (tag.x != cur) {
+      const int r = tag.x % QD;
+      cur = tag.x;
+      t.i = sQe[r].i;
+      t.h = sQe[r].h;
+      t.len = sQe[r].len;
+      t.apg = sQe[r].apg;
+      sQ = sRows + r * E;
     }
-
-    if (hdr.npg > 0) {
-      const int ntok = hdr.ntok;
-      const int nsteps = (ntok + 31) >> 5;
-      const uint32_t* sK = reinterpret_cast<const uint32_t*>(stage);
-      const float4* sQ4 = reinterpret_cast<const float4*>(sQ);
-      float x[kDecodeMaxChunkTokens / 32];
-      float mc = -INFINITY;
-#pragma unroll
-      for (int st = 0; st < kDecodeMaxChunkTokens / 32; ++st) {
-        x[st] = -INFINITY;
-        if (st < nsteps) {
-          const int j = st * 32 + lane;
-          const int jj = min(j, ntok - 1);
-          const int pg = jj / p.page, t = jj - pg * p.page;
-          const uint32_t* kp = sK + pg * ksw + t;
-          float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-          if constexpr (Tile::kBF) {
-#pragma unroll 8
-            for (int r = 0; r < Tile::kRows; r += 2) {
-              const uint32_t w0 = kp[r * p.page];
-              const uint32_t w1 = kp[(r + 1) * p.page];
-              const float4 qq = sQ4[r >> 1];
-              a0 = fmaf(bf16_lo(w0), qq.x, a0);
-              a1 = fmaf(bf16_hi(w0), qq.y, a1);
-              a2 = fmaf(bf16_lo(w1), qq.z, a2);
-              a3 = fmaf(bf16_hi(w1), qq.w, a3);
-            }
-          } else {
-            const float* kf = reinterpret_cast<const float*>(kp);
-#pragma unroll 8
-            for (int r = 0; r < Tile::kRows; r += 4) {
-              const float4 qq = sQ4[r >> 2];
-              a0 = fmaf(kf[r * p.page], qq.x, a0);
-              a1 = fmaf(kf[(r + 1) * p.page], qq.y, a1);
-              a2 = fmaf(kf[(r + 2) * p.page], qq.z, a2);
-              a3 = fmaf(kf[(r + 3) * p.page], qq.w, a3);
-            }
+    const float4* sQ4 = reinterpret_cast<const float4*>(sQ);
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    float m, lpart = 0.f;
+    {
+      const uint32_t parity = (cidx / (unsigned)p.stages) & 1u;
+      if (!decode_wait(&sBar[s], parity, sAbort)) {
+        failed = true;
+        fail_idx = cidx;
+        break;
+      }
+      uint8_t* stage = wbase + (size_t)s * p.stage_bytes;
+      const int pg = tag.y;
+      const int ntok = min(p.page, t.len - pg * p.page);
+      if (pg == t.apg) {
+        // the appended token: into the staged page (shared) and the cache
+        // (global), K transposed as the page layout wants, V as a row
+        const int tt = (t.len - 1) - pg * p.page;
+        const T* kn = static_cast<const T*>(p.k_new) + (long long)t.i * p.kv_stride + (long long)t.h * E;
+        const T* vn = static_cast<const T*>(p.v_new) + (long long)t.i * p.kv_stride + (long long)t.h * E;
+        int gblk = __ldg(p.page_table + (long long)t.i * p.pt_stride + pg);
+        if (gblk < 0 || gblk >= p.num_blocks) gblk = -1;
+        T* sKe = reinterpret_cast<T*>(stage);
+        T* sVt = reinterpret_cast<T*>(stage + p.kslot_bytes) + (size_t)tt * E;
+        const long long pbase = gblk >= 0 ? ((long long)gblk * p.H + t.h) * (long long)p.page * E : 0;
+        T* gK = static_cast<T*>(const_cast<void*>(p.kc)) + pbase;
+        T* gV = static_cast<T*>(const_cast<void*>(p.vc)) + pbase + (long long)tt * E;
+        for (int d = lane; d < E; d += 32) {
+          const T kv = kn[d], vv = vn[d];
+          const int ko = Tile::kBF ? (((d >> 1) * p.page + tt) * 2 + (d & 1)) : (d * p.page + tt);
+          sKe[ko] = kv;
+          sVt[d] = vv;
+          if (gblk >= 0) {
+            gK[ko] = kv;
+            gV[d] = vv;
           }
-          const float logit = (a0 + a1) + (a2 + a3);
-          x[st] = (j < ntok) ? logit * p.c : -INFINITY;
-          mc = fmaxf(mc, x[st]);
         }
+        __syncwarp();
       }
-      mc = warp_max(mc);
-      const float mn = fmaxf(m, mc);
-      const float alpha = exp2_approx(m - mn);
-      m = mn;
-      float ps = 0.f;
-#pragma unroll
-      for (int st = 0; st < kDecodeMaxChunkTokens / 32; ++st) {
-        if (st < nsteps) {
-          const float pr = exp2_approx(x[st] - mn);
-          sP[st * 32 + lane] = pr;
-          ps += pr;
-        }
-      }
-      lpart = fmaf(lpart, alpha, ps);
-#pragma unroll
-      for (int c = 0; c < 4; ++c) acc[c] *= alpha;
-      __syncwarp();
 
-      // P.V over exactly ntok keys
-      const uint32_t* sV = sK + p.cp * ksw;
-      for (int pg = 0; pg < hdr.npg; ++pg) {
-        const int tmax = min(p.page, ntok - pg * p.page);
-        const uint32_t* vb = sV + pg * vpage_words;
-        const float* pp = sP + pg * p.page;
+
+
+      // ---- Q.K^T for the page's ntok keys
+      const uint32_t* sK = reinterpret_cast<const uint32_t*>(stage);
+      const int nsteps = (ntok + 31) >> 5;
+      float x[kDecodeMaxPage / 32];
+#pragma unroll
+      for (int st = 0; st < kDecodeMaxPage / 32; ++st) x[st] = -INFINITY;
+      float mc = -INFINITY;
+      if (p.page == 16) {
+        // a 16-key page: lanes t and 16+t share key t, each half-warp takes
+        // every other K row (conflict-free: banks 16*half + t)
+        const int tk = lane & 15, hh = lane >> 4;
+        const uint32_t* kp = sK + tk;
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
         if constexpr (Tile::kBF) {
-#pragma unroll 4
-          for (int t = tg; t < tmax; t += Tile::kKeysPerStep) {
-            const float pj = pp[t];
-            const uint2 w = *reinterpret_cast<const uint2*>(vb + t * vrow_words + dg * 2);
-            acc[0] = fmaf(pj, bf16_lo(w.x), acc[0]);
-            acc[1] = fmaf(pj, bf16_hi(w.x), acc[1]);
-            acc[2] = fmaf(pj, bf16_lo(w.y), acc[2]);
-            acc[3] = fmaf(pj, bf16_hi(w.y), acc[3]);
+          const float2* sQ2 = reinterpret_cast<const float2*>(sQ);
+#pragma unroll 8
+          for (int r = hh; r < Tile::kRows; r += 4) {
+            const uint32_t w0 = kp[r * 16];
+            const uint32_t w1 = kp[(r + 2) * 16];
+            const float2 q0 = sQ2[r], q1 = sQ2[r + 2];
+            a0 = fmaf(bf16_lo(w0), q0.x, a0);
+            a1 = fmaf(bf16_hi(w0), q0.y, a1);
+            a2 = fmaf(bf16_lo(w1), q1.x, a2);
+            a3 = fmaf(bf16_hi(w1), q1.y, a3);
           }
         } else {
-#pragma unroll 4
-          for (int t = tg; t < tmax; t += Tile::kKeysPerStep) {
-            const float pj = pp[t];
-            const float4 w = *reinterpret_cast<const float4*>(vb + t * vrow_words + dg * 4);
-            acc[0] = fmaf(pj, w.x, acc[0]);
-            acc[1] = fmaf(pj, w.y, acc[1]);
-            acc[2] = fmaf(pj, w.z, acc[2]);
-            acc[3] = fmaf(pj, w.w, acc[3]);
+          const float* kf = reinterpret_cast<const float*>(kp);
+#pragma unroll 8
+          for (int r = hh; r < Tile::kRows; r += 8) {
+            a0 = fmaf(kf[r * 16], sQ[r], a0);
+            a1 = fmaf(kf[(r + 2) * 16], sQ[r + 2], a1);
+            a2 = fmaf(kf[(r + 4) * 16], sQ[r + 4], a2);
+            a3 = fmaf(kf[(r + 6) * 16], sQ[r + 6], a3);
           }
         }
-      }
-    }
-    __syncwarp();  // every lane is done with stage s
-
-    const int hflags = hdr.flags;
-    produce(s);  // refill stage s, stages-1 chunks ahead
-
-    if (hflags & kLast) {
-      // ---- end of a piece: reduce over the keys each lane group held
-      const float l = warp_sum(lpart);
-#pragma unroll
-      for (int o = Tile::kLanesPerKey; o < 32; o <<= 1) {
-#pragma unroll
-        for (int c = 0; c < 4; ++c) acc[c] += __shfl_xor_sync(0xffffffffu, acc[c], o);
-      }
-      T* orow = obase + (long long)hdr.i * p.out_stride + (long long)hdr.h * E;
-      if (hflags & kWhole) {
-        if (lane < Tile::kLanesPerKey) {
-          const float inv = l > 0.f ? 1.f / l : 0.f;
-#pragma unroll
-          for (int c = 0; c < 4; ++c) orow[dg * 4 + c] = from_f32<T>(l > 0.f ? acc[c] * inv : 0.f);
-        }
+        float logit = (a0 + a1) + (a2 + a3);
+        logit += __shfl_xor_sync(0xffffffffu, logit, 16);
+        x[0] = (tk < ntok && hh == 0) ? logit * p.c : -INFINITY;
+        mc = x[0];
       } else {
-        float* slot = p.partial + (long long)hdr.slot * (E + 2);
-        if (lane < Tile::kLanesPerKey) {
 #pragma unroll
-          for (int c = 0; c < 4; ++c) slot[2 + dg * 4 + c] = acc[c];
-        }
-        if (lane == 0) {
-          slot[0] = m;
-          slot[1] = l;
-        }
-        __threadfence();
-        __syncwarp();
-        int ticket = 0;
-        int* tk = p.tickets + (long long)hdr.i * p.H + hdr.h;
-        if (lane == 0) ticket = atomicAdd(tk, 1);
-        ticket = __shfl_sync(0xffffffffu, ticket, 0);
-        const long long ux = hdr.ux, uend = hdr.ux + hdr.np + 1;
-        const long long k0 = worker_of(ux, P, G), k1 = worker_of(uend - 1, P, G);
-        if (ticket == (int)(k1 - k0)) {
-          // the last piece to finish merges all of them
-          __threadfence();
-          float M = -INFINITY;
-          for (long long kk = k0; kk <= k1; ++kk) {
-            const long long sl = 2 * kk + ((kk == k0 && range_start(kk, P, G) < ux) ? 1 : 0);
-            M = fmaxf(M, __ldcg(p.partial + sl * (E + 2)));
-          }
-          float L = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
-          if (M != -INFINITY) {
-            for (long long kk = k0; kk <= k1; ++kk) {
-              const long long sl = 2 * kk + ((kk == k0 && range_start(kk, P, G) < ux) ? 1 : 0);
-              const float* ps = p.partial + sl * (E + 2);
-              const float w = exp2_approx(__ldcg(ps) - M);
-              L = fmaf(__ldcg(ps + 1), w, L);
-              if (lane < Tile::kLanesPerKey) {
-#pragma unroll
-                for (int c = 0; c < 4; ++c) o[c] = fmaf(__ldcg(ps + 2 + dg * 4 + c), w, o[c]);
+        for (int st = 0; st < kDecodeMaxPage / 32; ++st) {
+          if (st < nsteps) {
+            const int j = st * 32 + lane;
+            const uint32_t* kp = sK + min(j, ntok - 1);
+            float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+            if constexpr (Tile::kBF) {
+#pragma unroll 8
+              for (int r = 0; r < Tile::kRows; r += 2) {
+                const uint32_t w0 = kp[r * p.page];
+                const uint32_t w1 = kp[(r + 1) * p.page];
+                const float4 qq = sQ4[r >> 1];
+                a0 = fmaf(bf16_lo(w0), qq.x, a0);
+                a1 = fmaf(bf16_hi(w0), qq.y, a1);
+                a2 = fmaf(bf16_lo(w1), qq.z, a2);
+                a3 = fmaf(bf16_hi(w1), qq.w, a3);
+              }
+            } else {
+              const float* kf = reinterpret_cast<const float*>(kp);
+#pragma unroll 8
+              for (int r = 0; r < Tile::kRows; r += 4) {
+                const float4 qq = sQ4[r >> 2];
+                a0 = fmaf(kf[r * p.page], qq.x, a0);
+                a1 = fmaf(kf[(r + 1) * p.page], qq.y, a1);
+                a2 = fmaf(kf[(r + 2) * p.page], qq.z, a2);
+                a3 = fmaf(kf[(r + 3) * p.page], qq.w, a3);
               }
             }
+            const float logit = (a0 + a1) + (a2 + a3);
+            x[st] = (j < ntok) ? logit * p.c : -INFINITY;
+            mc = fmaxf(mc, x[st]);
           }
-          if (lane < Tile::kLanesPerKey) {
-            const float inv = L > 0.f ? 1.f / L : 0.f;
-#pragma unroll
-            for (int c = 0; c < 4; ++c) orow[dg * 4 + c] = from_f32<T>(L > 0.f ? o[c] * inv : 0.f);
-          }
-          if (lane == 0) *tk = 0;  // ready for the next call
         }
       }
+      // ---- softmax of the page on its own maximum
+      m = warp_max(mc);
+#pragma unroll
+      for (int st = 0; st < kDecodeMaxPage / 32; ++st) {
+        if (st < nsteps) {
+          const float pr = exp2_approx(x[st] - m);
+          sP[st * 32 + lane] = pr;
+          lpart += pr;
+        }
+      }
+      __syncwarp();
+      // ---- P.V over exactly ntok keys
+      const uint32_t* vb = reinterpret_cast<const uint32_t*>(stage + p.kslot_bytes);
+      if constexpr (Tile::kBF) {
+#pragma unroll 4
+        for (int tt = tg; tt < ntok; tt += Tile::kKeysPerStep) {
+          const float pj = sP[tt];
+          const uint2 wv = *reinterpret_cast<const uint2*>(vb + tt * vrow_words + dg * 2);
+          acc[0] = fmaf(pj, bf16_lo(wv.x), acc[0]);
+          acc[1] = fmaf(pj, bf16_hi(wv.x), acc[1]);
+          acc[2] = fmaf(pj, bf16_lo(wv.y), acc[2]);
+          acc[3] = fmaf(pj, bf16_hi(wv.y), acc[3]);
+        }
+      } else {
+#pragma unroll 4
+        for (int tt = tg; tt < ntok; tt += Tile::kKeysPerStep) {
+          const float pj = sP[tt];
+          const float4 wv = *reinterpret_cast<const float4*>(vb + tt * vrow_words + dg * 4);
+          acc[0] = fmaf(pj, wv.x, acc[0]);
+          acc[1] = fmaf(pj, wv.y, acc[1]);
+          acc[2] = fmaf(pj, wv.z, acc[2]);
+          acc[3] = fmaf(pj, wv.w, acc[3]);
+        }
+      }
+      __syncwarp();  // every lane is done with stage s
+      ++cidx;
     }
+    produce();  // the stage is free: refill it before depositing
+    // ---- deposit the page's state in slot tag.z % R once the merger is past
+    // the page that held it before
+    const float l = warp_sum(lpart);
+#pragma unroll
+    for (int o = Tile::kLanesPerKey; o < 32; o <<= 1) {
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) acc[cc] += __shfl_xor_sync(0xffffffffu, acc[cc], o);
+    }
+    const int gz = tag.z;
+    if (!spin_until([&] { return *sMergedPages > gz - R; }, sAbort)) {
+      failed = true;
+      fail_idx = cidx;
+      break;
+    }
+    float* slot = sPage + (gz % R) * (E + 4);
+    if (lane < Tile::kLanesPerKey) *reinterpret_cast<float4*>(slot + dg * 4) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    if (lane == 0) {
+      slot[E] = m;
+      slot[E + 1] = l;
+    }
+    __syncwarp();
+    __threadfence_block();
+    if (lane == 0) sFlag[gz % R] = gz;
   }
+  if (failed && lane == 0) {
+    atomicOr(p.status, CA_STATUS_TIMEOUT);
+    *sAbort = 1;
+  }
+  // copies still in flight (only after a timeout): one more bounded chance
+  if (failed)
+    for (unsigned r = fail_idx; r < pidx; ++r)
+      mbar_wait_bounded(&sBar[r % p.stages], (r / p.stages) & 1u, kWaitLimitNs);
 }
 
 }  // namespace ca

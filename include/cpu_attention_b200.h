@@ -117,7 +117,7 @@ CA_API int ca_decode(const void* q, int64_t q_stride, void* k_cache, void* v_cac
  * workspace: it runs ca_decode with a static device array of the library as
  * the workspace and allocates nothing.
  * Limits: batch * heads <= 65536 and at most 160 SMs, else CA_ESCRATCH and
- *   nothing is launched. The array (about 1.6 MiB) stays resident on every
+ *   nothing is launched. The array (about 5.3 MiB) stays resident on every
  *   GPU that loads the library until the process exits.
  * Every call shares the array: calls that overlap on the GPU race; order them.
  *   Device-found value errors are skipped but not reported (validate on the
