@@ -367,6 +367,13 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
+# DRAM bytes (read + write) of one launch of the roofline kernel, from one ncu
+# capture of the same command (the files under profiles/ give the commands).
+TRAFFIC = {
+    "cfg2": (283.1e6, "profiles/decode_kernel_cfg2.md"),
+    "cfg4": (251.1e6, "profiles/flash_tc_kernel_cfg4.md"),
+}
+
 HOST_HIDE_CYCLES = 400_000  # ~0.2 ms of device spin: longer than the host needs to enqueue one step
 
 
@@ -532,7 +539,9 @@ def main():
         peak, bound, runit = pk["hbm_gbs"], "hbm", "GB/s"
     achieved = max_over_ranks(-achieved, world) * -1  # the slowest rank
     roofline = {"bound": bound, "achieved": round(achieved, 2), "peak": peak, "peak_kind": pk_kind,
-                "unit": runit, "frac": round(achieved / peak, 4), "traffic": None,
+                "unit": runit, "frac": round(achieved / peak, 4),
+                "traffic": TRAFFIC[args.workload][0] if args.workload in TRAFFIC else None,
+                "traffic_source": TRAFFIC[args.workload][1] if args.workload in TRAFFIC else None,
                 "kernel_ms": round(kern_avg, 4)}
 
     # end to end through the public API, host buffers
