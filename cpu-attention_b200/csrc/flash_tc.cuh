@@ -8,19 +8,24 @@
 // slack the reference's AMX policy uses (`flash_amx.mojo:37`, `:469-475`), so
 // most tiles rescale nothing; probabilities then stay below 2^8.
 //
-// One CTA = 128 query rows of one (batch, head), 6 warps:
-//   warp 0     TMA producer: Q once, then K and V tiles of 128 keys into a
-//              ring of STAGES slots (128B-swizzled, or 64B for head_dim 32)
-//   warp 1     allocates 512 TMEM columns; lane 0 issues the MMAs:
-//                S_j = Q K_j^T   (M=128, N=128, K=E; both operands K-major, smem)
-//                O  += P_j V_j   (M=128, N=E,  K=128; P from TMEM, V MN-major)
-//              S_{j+1} is issued before O += P_j V_j, so the tensor core works
-//              on the next tile while the softmax warps work on this one.
-//   warps 2-5  softmax: thread = query row = TMEM lane. Read S_j from TMEM,
-//              mask, online softmax in log2 units, write bf16 P_j to TMEM,
-//              rescale O when the max moved, and finally O / l -> global.
-// TMEM columns: S double buffer [0,128) [128,256), P double buffer [256,320)
-// [320,384) (bf16 pairs), O [384, 384+E).
+// One CTA = two 128-row query tiles (A, B) of one (batch, head) sharing every
+// K/V tile, 12 warps in three warpgroups:
+//   warp 0     TMA: Q_A and Q_B once, then K and V tiles of 128 keys into two
+//              rings (128B-swizzled rows, 64B at head_dim 32)
+//   warp 1     allocates the SM's 512 TMEM columns; lane 0 issues the MMAs
+//                S_X = Q_X K_j^T  (M=128, N=128, K=E; both operands K-major)
+//                O_X += P_X V_j   (M=128, N=E, K=128; P from TMEM, V MN-major)
+//              in the order S_A S_B | PV_A(j) S_A(j+1) | PV_B(j) S_B(j+1) ...,
+//              so the tensor core works on one tile while the other tile's
+//              softmax runs (ping-pong).
+//   warps 2-3  idle (their registers go to the softmax warpgroups)
+//   warps 4-7  softmax of tile A, warps 8-11 of tile B: thread = query row =
+//              TMEM lane. The S row comes into registers in one TMEM round
+//              trip, the row max is taken, bf16 P is written back over the S
+//              columns; O is rescaled only when the max moved; finally
+//              O / l -> global.
+// TMEM columns: S_A [0,128) (P_A over its first 64), O_A [128,128+E),
+// S_B [256,384) (P_B), O_B [384,384+E).
 #pragma once
 
 #include <cuda.h>
@@ -40,24 +45,32 @@ struct FlashTcArgs {
 
 template <int E>
 struct TcCfg {
-  static constexpr int BM = 128, BN = 128;
-  static constexpr int SWB = E >= 64 ? 128 : 64;  // swizzle row bytes
-  static constexpr int CHUNK = SWB / 2;           // elements per swizzle row
-  static constexpr int NCH = E / CHUNK;           // TMA boxes per tile along the head dim
-  static constexpr int CH_BYTES = 128 * SWB;      // one box: 128 rows
+  static constexpr int BM = 128, BN = 128, ROWS = 256;  // rows per tile, keys per tile, rows per CTA
+  static constexpr int SWB = E >= 64 ? 128 : 64;        // swizzle row bytes
+  static constexpr int CHUNK = SWB / 2;                 // elements per swizzle row
+  static constexpr int NCH = E / CHUNK;                 // TMA boxes per tile along the head dim
+  static constexpr int CH_BYTES = 128 * SWB;            // one box: 128 rows
   static constexpr int TILE_BYTES = NCH * CH_BYTES;
-  static constexpr int STAGES = E == 128 ? 2 : (E == 64 ? 3 : 4);
+  static constexpr int KST = E == 128 ? 3 : 4;  // K ring
+  static constexpr int VST = E == 128 ? 2 : 4;  // V ring
   static constexpr uint32_t SWZ = E >= 64 ? tc::kSwizzle128 : tc::kSwizzle64;
-  static constexpr int T_S0 = 0, T_P0 = 256, T_O = 384, TMEM_COLS = 512;
-  static constexpr int SMEM_TILES = TILE_BYTES * (1 + 2 * STAGES);
+  // TMEM column of tile x's S (and P) and of its O
+  static __device__ __forceinline__ constexpr uint32_t T_S(int x) { return (uint32_t)x * 256; }
+  static __device__ __forceinline__ constexpr uint32_t T_O(int x) { return 128u + (uint32_t)x * 256; }
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int SMEM_TILES = TILE_BYTES * (2 + KST + VST);
   // 1024 B alignment slack + barriers; at least ~116 KB so that one CTA holds
   // an SM (its 512 TMEM columns are the whole SM's)
   static constexpr int SMEM_BYTES = (SMEM_TILES + 1024 + 256) > 118784 ? (SMEM_TILES + 1024 + 256) : 118784;
   static constexpr float SLACK = 8.0f;
+  // 384 threads launched with REGS_LAUNCH registers each; warps 0-3 (TMA,
+  // MMA, two idle) drop to REGS_PRODUCER and the two softmax warpgroups rise
+  // to REGS_SOFTMAX: 128 * 48 + 256 * 224 <= 384 * 168
+  static constexpr int THREADS = 384, REGS_LAUNCH = 168, REGS_PRODUCER = 48, REGS_SOFTMAX = 224;
 };
 
 struct TcBars {
-  uint64_t q, k[4], v[4], empty[4], s[2], p[2], pv[2], fin;
+  uint64_t q, kf[4], ke[4], vf[4], ve[4], s[2], p[2], pv[2], fin;
   uint32_t tmem;
   int abort;
 };
@@ -83,32 +96,78 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// Packed fp32 pairs (sm_100 f32x2 arithmetic) and a 3-input max.
+__device__ __forceinline__ uint64_t f32x2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float lo_f32(uint64_t v) {
+  float lo;
+  asm("{\n\t.reg .f32 t;\n\tmov.b64 {%0, t}, %1;\n\t}" : "=f"(lo) : "l"(v));
+  return lo;
+}
+__device__ __forceinline__ float hi_f32(uint64_t v) {
+  float hi;
+  asm("{\n\t.reg .f32 t;\n\tmov.b64 {t, %0}, %1;\n\t}" : "=f"(hi) : "l"(v));
+  return hi;
+}
+__device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+__device__ __forceinline__ float fmin3(float a, float b, float c) {
+  float r;
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// Number of 128-key tiles rows [r0, r0+128) need (0 when none of them exists
+// or sees a key).
+__device__ __forceinline__ int tc_tiles(int r0, int Lq, int Lk, bool causal) {
+  if (r0 >= Lq) return 0;
+  const int kend = causal ? min(Lk, min(r0 + 128, Lq) + Lk - Lq) : Lk;
+  return kend > 0 ? (kend + 127) / 128 : 0;
+}
+
 template <int E, bool CAUSAL>
-__global__ void __launch_bounds__(192, 1) flash_tc_kernel(const __grid_constant__ FlashTcArgs a) {
+__global__ void __launch_bounds__(384, 1) flash_tc_kernel(const __grid_constant__ FlashTcArgs a) {
   using C = TcCfg<E>;
   extern __shared__ __align__(1024) uint8_t tc_smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = sm;
-  uint8_t* sK = sm + C::TILE_BYTES;
-  uint8_t* sV = sK + C::STAGES * C::TILE_BYTES;
-  TcBars* bars = reinterpret_cast<TcBars*>(sV + C::STAGES * C::TILE_BYTES);
+  uint8_t* sQ = sm;  // [2][TILE]
+  uint8_t* sK = sm + 2 * C::TILE_BYTES;
+  uint8_t* sV = sK + C::KST * C::TILE_BYTES;
+  TcBars* bars = reinterpret_cast<TcBars*>(sV + C::VST * C::TILE_BYTES);
   volatile int* abort = &bars->abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nqt = (a.Lq + C::BM - 1) / C::BM;
-  const int qt = CAUSAL ? nqt - 1 - (int)blockIdx.x : (int)blockIdx.x;  // heavy causal tiles first
+  const int nblk = (a.Lq + C::ROWS - 1) / C::ROWS;
+  const int blk = CAUSAL ? nblk - 1 - (int)blockIdx.x : (int)blockIdx.x;  // heavy causal blocks first
   const int h = blockIdx.y, b = blockIdx.z;
-  const int q0 = qt * C::BM;
-  const int diag = a.Lk - a.Lq;
-  int kend = CAUSAL ? min(a.Lk, q0 + C::BM + diag) : a.Lk;
-  const int nt = kend > 0 ? (kend + C::BN - 1) / C::BN : 0;
+  const int q0 = blk * C::ROWS;
+  const int nt0 = tc_tiles(q0, a.Lq, a.Lk, CAUSAL), nt1 = tc_tiles(q0 + C::BM, a.Lq, a.Lk, CAUSAL);
+  const int nt = max(nt0, nt1);
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q, 1);
-    for (int s = 0; s < C::STAGES; ++s) {
-      mbar_init(&bars->k[s], 1);
-      mbar_init(&bars->v[s], 1);
-      mbar_init(&bars->empty[s], 1);
+    for (int s = 0; s < 4; ++s) {
+      mbar_init(&bars->kf[s], 1);
+      mbar_init(&bars->ke[s], 1);
+      mbar_init(&bars->vf[s], 1);
+      mbar_init(&bars->ve[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bars->s[s], 1);
@@ -125,160 +184,185 @@ __global__ void __launch_bounds__(192, 1) flash_tc_kernel(const __grid_constant_
   tc::fence_after_sync();
   const uint32_t tmem = bars->tmem;
 
+  if (warp < 4) tc::reg_dealloc<C::REGS_PRODUCER>();
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA
     if (lane == 0 && nt > 0) {
       tc::prefetch_tmap(&a.tq);
       tc::prefetch_tmap(&a.tk);
       tc::prefetch_tmap(&a.tv);
-      mbar_arrive_expect_tx(&bars->q, C::TILE_BYTES);
+      const int nq = nt1 > 0 ? 2 : 1;
+      mbar_arrive_expect_tx(&bars->q, nq * C::TILE_BYTES);
+      for (int x = 0; x < nq; ++x)
 #pragma unroll
-      for (int ch = 0; ch < C::NCH; ++ch)
-        tc::tma_load_4d(sQ + ch * C::CH_BYTES, &a.tq, ch * C::CHUNK, q0, h, b, &bars->q);
+        for (int ch = 0; ch < C::NCH; ++ch)
+          tc::tma_load_4d(sQ + x * C::TILE_BYTES + ch * C::CH_BYTES, &a.tq, ch * C::CHUNK, q0 + x * C::BM, h, b,
+                          &bars->q);
+      // K runs ahead of V: K_j is needed by S(j), V_j only by the later PV(j)
+      int jv = 0;
       for (int j = 0; j < nt; ++j) {
-        const int st = j % C::STAGES;
-        if (j >= C::STAGES && !tc_wait(&bars->empty[st], ((j / C::STAGES) - 1) & 1, abort, a.status)) break;
-        uint8_t* kd = sK + st * C::TILE_BYTES;
-        uint8_t* vd = sV + st * C::TILE_BYTES;
-        mbar_arrive_expect_tx(&bars->k[st], C::TILE_BYTES);
+        const int ks = j % C::KST;
+        if (j >= C::KST && !tc_wait(&bars->ke[ks], ((j / C::KST) - 1) & 1, abort, a.status)) break;
+        mbar_arrive_expect_tx(&bars->kf[ks], C::TILE_BYTES);
 #pragma unroll
         for (int ch = 0; ch < C::NCH; ++ch)
-          tc::tma_load_4d(kd + ch * C::CH_BYTES, &a.tk, ch * C::CHUNK, j * C::BN, h, b, &bars->k[st]);
-        mbar_arrive_expect_tx(&bars->v[st], C::TILE_BYTES);
+          tc::tma_load_4d(sK + ks * C::TILE_BYTES + ch * C::CH_BYTES, &a.tk, ch * C::CHUNK, j * C::BN, h, b,
+                          &bars->kf[ks]);
+        // the V tiles whose slot is free by now
+        for (; jv <= j; ++jv) {
+          const int vs = jv % C::VST;
+          if (jv >= C::VST && !mbar_try_wait(&bars->ve[vs], ((jv / C::VST) - 1) & 1)) break;
+          mbar_arrive_expect_tx(&bars->vf[vs], C::TILE_BYTES);
+#pragma unroll
+          for (int ch = 0; ch < C::NCH; ++ch)
+            tc::tma_load_4d(sV + vs * C::TILE_BYTES + ch * C::CH_BYTES, &a.tv, ch * C::CHUNK, jv * C::BN, h, b,
+                            &bars->vf[vs]);
+        }
+      }
+      for (; jv < nt && !*abort; ++jv) {
+        const int vs = jv % C::VST;
+        if (jv >= C::VST && !tc_wait(&bars->ve[vs], ((jv / C::VST) - 1) & 1, abort, a.status)) break;
+        mbar_arrive_expect_tx(&bars->vf[vs], C::TILE_BYTES);
 #pragma unroll
         for (int ch = 0; ch < C::NCH; ++ch)
-          tc::tma_load_4d(vd + ch * C::CH_BYTES, &a.tv, ch * C::CHUNK, j * C::BN, h, b, &bars->v[st]);
+          tc::tma_load_4d(sV + vs * C::TILE_BYTES + ch * C::CH_BYTES, &a.tv, ch * C::CHUNK, jv * C::BN, h, b,
+                          &bars->vf[vs]);
       }
       // leave only after every load this CTA issued has landed
-      for (int j = max(0, nt - C::STAGES); j < nt; ++j) {
-        const int st = j % C::STAGES;
-        tc_wait(&bars->k[st], (j / C::STAGES) & 1, abort, nullptr);
-        tc_wait(&bars->v[st], (j / C::STAGES) & 1, abort, nullptr);
-      }
+      for (int j = max(0, nt - C::KST); j < nt; ++j)
+        tc_wait(&bars->kf[j % C::KST], (j / C::KST) & 1, abort, nullptr);
+      for (int j = max(0, jv - C::VST); j < jv; ++j)
+        tc_wait(&bars->vf[j % C::VST], (j / C::VST) & 1, abort, nullptr);
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA
     if (lane == 0 && nt > 0) {
       constexpr uint32_t idS = tc::idesc_bf16(128, 128, 0);
       constexpr uint32_t idO = tc::idesc_bf16(128, E, 1);
-      const uint32_t qaddr = smem_u32(sQ);
       bool ok = tc_wait(&bars->q, 0, abort, a.status);
       tc::fence_after_sync();
-      auto issue_s = [&](int j) -> bool {
-        const int st = j % C::STAGES;
-        if (!tc_wait(&bars->k[st], (j / C::STAGES) & 1, abort, a.status)) return false;
+      // S_x(j) = Q_x K_j^T; the last user of K_j releases its slot
+      auto issue_s = [&](int x, int j) -> bool {
+        const int ks = j % C::KST;
+        if (!tc_wait(&bars->kf[ks], (j / C::KST) & 1, abort, a.status)) return false;
         tc::fence_after_sync();
-        const uint32_t kaddr = smem_u32(sK + st * C::TILE_BYTES);
-        const uint32_t d = tmem + C::T_S0 + (j & 1) * 128;
+        const uint32_t qaddr = smem_u32(sQ + x * C::TILE_BYTES);
+        const uint32_t kaddr = smem_u32(sK + ks * C::TILE_BYTES);
 #pragma unroll
-        for (int ks = 0; ks < E / 16; ++ks) {
-          const uint32_t off = (ks / (C::CHUNK / 16)) * C::CH_BYTES + (ks % (C::CHUNK / 16)) * 32;
-          const uint64_t ad = tc::smem_desc(qaddr + off, 16, 8 * C::SWB, C::SWZ);
-          const uint64_t bd = tc::smem_desc(kaddr + off, 16, 8 * C::SWB, C::SWZ);
-          tc::mma_ss(d, ad, bd, idS, ks > 0 ? 1u : 0u);
+        for (int kk = 0; kk < E / 16; ++kk) {
+          const uint32_t off = (kk / (C::CHUNK / 16)) * C::CH_BYTES + (kk % (C::CHUNK / 16)) * 32;
+          tc::mma_ss(tmem + C::T_S(x), tc::smem_desc(qaddr + off, 16, 8 * C::SWB, C::SWZ),
+                     tc::smem_desc(kaddr + off, 16, 8 * C::SWB, C::SWZ), idS, kk > 0 ? 1u : 0u);
         }
-        tc::commit(&bars->s[j & 1]);
+        tc::commit(&bars->s[x]);
+        if (x == 1 || j >= nt1) tc::commit(&bars->ke[ks]);
         return true;
       };
-      auto issue_pv = [&](int i) -> bool {
-        const int st = i % C::STAGES;
-        if (!tc_wait(&bars->p[i & 1], (i >> 1) & 1, abort, a.status)) return false;
-        if (!tc_wait(&bars->v[st], (i / C::STAGES) & 1, abort, a.status)) return false;
+      // O_x += P_x(j) V_j; the last user of V_j releases its slot
+      auto issue_pv = [&](int x, int j) -> bool {
+        const int vs = j % C::VST;
+        if (!tc_wait(&bars->p[x], j & 1, abort, a.status)) return false;
+        if (!tc_wait(&bars->vf[vs], (j / C::VST) & 1, abort, a.status)) return false;
         tc::fence_after_sync();
-        const uint32_t vaddr = smem_u32(sV + st * C::TILE_BYTES);
+        const uint32_t vaddr = smem_u32(sV + vs * C::TILE_BYTES);
 #pragma unroll
-        for (int ks = 0; ks < C::BN / 16; ++ks) {
-          const uint64_t bd = tc::smem_desc(vaddr + ks * 16 * C::SWB, C::CH_BYTES, 8 * C::SWB, C::SWZ);
-          tc::mma_ts(tmem + C::T_O, tmem + C::T_P0 + (i & 1) * 64 + ks * 8, bd, idO, (i > 0 || ks > 0) ? 1u : 0u);
-        }
-        tc::commit(&bars->empty[st]);
-        tc::commit(&bars->pv[i & 1]);
+        for (int kk = 0; kk < C::BN / 16; ++kk)
+          tc::mma_ts(tmem + C::T_O(x), tmem + C::T_S(x) + kk * 8,
+                     tc::smem_desc(vaddr + kk * 16 * C::SWB, C::CH_BYTES, 8 * C::SWB, C::SWZ), idO,
+                     (j > 0 || kk > 0) ? 1u : 0u);
+        tc::commit(&bars->pv[x]);
+        if (x == 1 || j >= nt1) tc::commit(&bars->ve[vs]);
         return true;
       };
-      if (ok) ok = issue_s(0);
-      for (int j = 1; ok && j < nt; ++j) {
-        ok = issue_s(j);
-        if (ok) ok = issue_pv(j - 1);
+      if (ok && nt0 > 0) ok = issue_s(0, 0);
+      if (ok && nt1 > 0) ok = issue_s(1, 0);
+      for (int j = 0; ok && j < nt; ++j) {
+        for (int x = 0; ok && x < 2; ++x) {
+          if (j >= (x ? nt1 : nt0)) continue;
+          ok = issue_pv(x, j);
+          // S_x(j+1) overwrites S_x/P_x: issued after PV_x(j), tcgen05.mma runs in order
+          if (ok && j + 1 < (x ? nt1 : nt0)) ok = issue_s(x, j + 1);
+        }
       }
-      if (ok) issue_pv(nt - 1);
       // every MMA this thread issued has retired before TMEM is released
       tc::commit(&bars->fin);
       mbar_wait_bounded(&bars->fin, 0, kWaitLimitNs);
     }
-  } else {
+  } else if (warp >= 4) {
     // ---------------------------------------------------------------- softmax
-    const int grp = warp & 3;  // TMEM lanes [32*grp, 32*grp+32)
+    tc::reg_alloc<C::REGS_SOFTMAX>();
+    const int x = (warp >> 2) - 1;  // query tile: warps 4-7 -> A, 8-11 -> B
+    const int grp = warp & 3;       // TMEM lanes [32*grp, 32*grp+32)
     const int r = grp * 32 + lane;
     const uint32_t lrow = tmem + ((uint32_t)(grp * 32) << 16);
-    const int qi = q0 + r;
-    const int lim = CAUSAL ? min(a.Lk - 1, qi + diag) : a.Lk - 1;  // last key this row sees
+    const uint32_t tS = lrow + C::T_S(x), tO = lrow + C::T_O(x);
+    const int qi = q0 + x * C::BM + r;
+    const int lim = CAUSAL ? min(a.Lk - 1, qi + a.Lk - a.Lq) : a.Lk - 1;  // last key this row sees
+    const int ntr = (x ? nt1 : nt0);
+    // masked scores get a value that scale * value maps to -inf
+    const float sent = a.c >= 0.f ? -INFINITY : INFINITY;
+    const uint64_t c2v = f32x2(a.c, a.c);
     float m = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; ok && j < nt; ++j) {
-      const int bb = j & 1;
-      if (!__all_sync(0xffffffffu, tc_wait(&bars->s[bb], (j >> 1) & 1, abort, a.status))) {
+    for (int j = 0; j < ntr; ++j) {
+      if (!__all_sync(0xffffffffu, tc_wait(&bars->s[x], j & 1, abort, a.status))) {
         ok = false;
         break;
       }
       tc::fence_after_sync();
-      float x[128];
+      // the whole S row in registers: one TMEM round trip per tile
+      uint32_t sr[C::BN];
 #pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
-        uint32_t rr[32];
-        tc::tmem_ld32(lrow + C::T_S0 + bb * 128 + c4 * 32, rr);
-        tc::tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) x[c4 * 32 + i] = __uint_as_float(rr[i]);
-      }
+      for (int c4 = 0; c4 < C::BN / 32; ++c4) tc::tmem_ld32(tS + c4 * 32, *reinterpret_cast<uint32_t(*)[32]>(sr + c4 * 32));
+      tc::tmem_ld_wait();
       const int k0 = j * C::BN;
       const bool full = (k0 + C::BN - 1) <= lim;
-      float mx = -INFINITY;
-      if (full) {
+      if (!full) {
 #pragma unroll
-        for (int i = 0; i < 128; ++i) {
-          x[i] *= a.c;
-          mx = fmaxf(mx, x[i]);
-        }
+        for (int i = 0; i < C::BN; ++i)
+          if (k0 + i > lim) sr[i] = __float_as_uint(sent);
+      }
+      float t = sent;
+      if (a.c >= 0.f) {
+#pragma unroll
+        for (int i = 0; i < C::BN; i += 2) t = fmax3(t, __uint_as_float(sr[i]), __uint_as_float(sr[i + 1]));
       } else {
 #pragma unroll
-        for (int i = 0; i < 128; ++i) {
-          x[i] = (k0 + i <= lim) ? x[i] * a.c : -INFINITY;
-          mx = fmaxf(mx, x[i]);
-        }
+        for (int i = 0; i < C::BN; i += 2) t = fmin3(t, __uint_as_float(sr[i]), __uint_as_float(sr[i + 1]));
       }
+      const float mx = t == sent ? -INFINITY : t * a.c;
       const bool need = mx > m + C::SLACK;
       const float mn = need ? mx : m;
       const float alpha = need ? exp2_approx(m - mn) : 1.f;  // m = -inf: 0
       const float mu = (mn == -INFINITY) ? 0.f : mn;         // a row with nothing visible yet
-      uint32_t pk[64];
-      float sum = 0.f;
+      // P = 2^(scale*s - m) as bf16 pairs, over the first BN/2 S columns
+      const uint64_t nm2 = f32x2(-mu, -mu);
+      uint64_t sum2 = f32x2(0.f, 0.f);
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const float p0 = exp2_approx(x[2 * i] - mu);
-        const float p1 = exp2_approx(x[2 * i + 1] - mu);
-        sum += p0 + p1;
-        pk[i] = tc::pack_bf16(p0, p1);
+      for (int ch = 0; ch < C::BN / 32; ++ch) {
+        // packed pair i of this chunk goes to sr[32ch + i]: it was read (as
+        // element 2i >= i of the chunk) before it is overwritten
+        uint32_t* pk = sr + ch * 32;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int e0 = ch * 32 + 2 * i;
+          const uint64_t xe = fma_f32x2(f32x2(__uint_as_float(sr[e0]), __uint_as_float(sr[e0 + 1])), c2v, nm2);
+          float p0 = exp2_approx(lo_f32(xe)), p1 = exp2_approx(hi_f32(xe));
+          if (!full) {
+            p0 = k0 + e0 <= lim ? p0 : 0.f;
+            p1 = k0 + e0 + 1 <= lim ? p1 : 0.f;
+          }
+          sum2 = add_f32x2(sum2, f32x2(p0, p1));
+          pk[i] = tc::pack_bf16(p0, p1);
+        }
+        tc::tmem_st16(tS + ch * 16, *reinterpret_cast<const uint32_t(*)[16]>(pk));
       }
+      const float sum = lo_f32(sum2) + hi_f32(sum2);
       l = fmaf(l, alpha, sum);
       m = mn;
-      // P_j goes where P_{j-2} was: PV_{j-2} must have read it
-      if (j >= 2 && !__all_sync(0xffffffffu, tc_wait(&bars->pv[bb], ((j - 2) >> 1) & 1, abort, a.status))) {
-        ok = false;
-        break;
-      }
-      {
-        uint32_t lo[32], hi[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          lo[i] = pk[i];
-          hi[i] = pk[32 + i];
-        }
-        tc::tmem_st32(lrow + C::T_P0 + bb * 64, lo);
-        tc::tmem_st32(lrow + C::T_P0 + bb * 64 + 32, hi);
-      }
       // rescale O (holding tiles < j) when the max moved
       if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.f)) {
-        if (!__all_sync(0xffffffffu, tc_wait(&bars->pv[(j - 1) & 1], ((j - 1) >> 1) & 1, abort, a.status))) {
+        if (!__all_sync(0xffffffffu, tc_wait(&bars->pv[x], (j - 1) & 1, abort, a.status))) {
           ok = false;
           break;
         }
@@ -286,42 +370,44 @@ __global__ void __launch_bounds__(192, 1) flash_tc_kernel(const __grid_constant_
 #pragma unroll
         for (int c4 = 0; c4 < E / 32; ++c4) {
           uint32_t rr[32];
-          tc::tmem_ld32(lrow + C::T_O + c4 * 32, rr);
+          tc::tmem_ld32(tO + c4 * 32, rr);
           tc::tmem_ld_wait();
 #pragma unroll
           for (int i = 0; i < 32; ++i) rr[i] = __float_as_uint(__uint_as_float(rr[i]) * alpha);
-          tc::tmem_st32(lrow + C::T_O + c4 * 32, rr);
+          tc::tmem_st32(tO + c4 * 32, rr);
         }
       }
       tc::tmem_st_wait();
       tc::fence_before_sync();
-      mbar_arrive(&bars->p[bb]);
+      mbar_arrive(&bars->p[x]);
     }
     // ---- epilogue: out = O / l (0 for a row that saw no key)
-    __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(a.out) + (((long long)b * a.Lq + qi) * a.H + h) * E;
-    const bool have = ok && nt > 0 &&
-                      __all_sync(0xffffffffu, tc_wait(&bars->pv[(nt - 1) & 1], ((nt - 1) >> 1) & 1, abort, a.status));
-    if (have) tc::fence_after_sync();
-    const float inv = l > 0.f ? 1.f / l : 0.f;
+    if (q0 + x * C::BM < a.Lq) {
+      __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(a.out) + (((long long)b * a.Lq + qi) * a.H + h) * E;
+      const bool have =
+          ok && ntr > 0 && __all_sync(0xffffffffu, tc_wait(&bars->pv[x], (ntr - 1) & 1, abort, a.status));
+      if (have) tc::fence_after_sync();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
 #pragma unroll
-    for (int c4 = 0; c4 < E / 32; ++c4) {
-      uint32_t rr[32];
-      if (have) {
-        tc::tmem_ld32(lrow + C::T_O + c4 * 32, rr);
-        tc::tmem_ld_wait();
-      }
-      if (qi < a.Lq) {
-        uint4 w[4];
-        uint32_t* wp = reinterpret_cast<uint32_t*>(w);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float o0 = (have && l > 0.f) ? __uint_as_float(rr[2 * i]) * inv : 0.f;
-          const float o1 = (have && l > 0.f) ? __uint_as_float(rr[2 * i + 1]) * inv : 0.f;
-          wp[i] = tc::pack_bf16(o0, o1);
+      for (int c4 = 0; c4 < E / 32; ++c4) {
+        uint32_t rr[32];
+        if (have) {
+          tc::tmem_ld32(tO + c4 * 32, rr);
+          tc::tmem_ld_wait();
         }
-        uint4* dst = reinterpret_cast<uint4*>(orow + c4 * 32);
+        if (qi < a.Lq) {
+          uint4 w[4];
+          uint32_t* wp = reinterpret_cast<uint32_t*>(w);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) dst[i] = w[i];
+          for (int i = 0; i < 16; ++i) {
+            const float o0 = (have && l > 0.f) ? __uint_as_float(rr[2 * i]) * inv : 0.f;
+            const float o1 = (have && l > 0.f) ? __uint_as_float(rr[2 * i + 1]) * inv : 0.f;
+            wp[i] = tc::pack_bf16(o0, o1);
+          }
+          uint4* dst = reinterpret_cast<uint4*>(orow + c4 * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) dst[i] = w[i];
+        }
       }
     }
   }
@@ -332,7 +418,6 @@ __global__ void __launch_bounds__(192, 1) flash_tc_kernel(const __grid_constant_
     tc::tmem_dealloc(tmem, C::TMEM_COLS);
   }
 }
-
 
 // ---------------------------------------------------------------------------
 // host side
@@ -397,6 +482,10 @@ int flash_tc_launch(const FlashParams& p, int* status, cudaStream_t stream, std:
   static bool configured[2] = {false, false};
   auto kern = p.causal ? flash_tc_kernel<E, true> : flash_tc_kernel<E, false>;
   if (!configured[p.causal]) {
+    // the register split assumes exactly REGS_LAUNCH registers per thread at
+    // launch (a larger split would wait forever in setmaxnreg)
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess || fa.numRegs != C::REGS_LAUNCH) return CA_EUNSUPPORTED;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
     if (e != cudaSuccess) {
       *err = std::string("cudaFuncSetAttribute(flash_tc): ") + cudaGetErrorString(e);
@@ -404,8 +493,8 @@ int flash_tc_launch(const FlashParams& p, int* status, cudaStream_t stream, std:
     }
     configured[p.causal] = true;
   }
-  dim3 grid((p.Lq + C::BM - 1) / C::BM, p.H, p.B);
-  kern<<<grid, 192, C::SMEM_BYTES, stream>>>(a);
+  dim3 grid((p.Lq + C::ROWS - 1) / C::ROWS, p.H, p.B);
+  kern<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     *err = std::string("flash_tc launch: ") + cudaGetErrorString(e);
