@@ -400,11 +400,16 @@ def timed(fn, steps, warmup, flush, stream, hide_host=True):
     return [a.elapsed_time(b) for a, b in evs]
 
 
+def _reduce_device():
+    import torch.distributed as dist
+    return "cuda" if dist.get_backend() == "nccl" else "cpu"
+
+
 def max_over_ranks(x, world):
     if world == 1:
         return x
     import torch.distributed as dist
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    t = torch.tensor([x], dtype=torch.float64, device=_reduce_device())
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 
@@ -413,7 +418,7 @@ def sum_over_ranks(x, world):
     if world == 1:
         return x
     import torch.distributed as dist
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    t = torch.tensor([x], dtype=torch.float64, device=_reduce_device())
     dist.all_reduce(t, op=dist.ReduceOp.SUM)
     return float(t.item())
 
