@@ -59,7 +59,7 @@ namespace ca {
 constexpr int kDecodeMaxPage = 128;               // tokens per page this kernel stages
 constexpr int kKSlotPadBytes = 64;                // K page slot padding: 16 banks
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s per bounded wait
-constexpr int kDecodeMaxWarps = 10;               // streaming warps per CTA (plus a merger and a feeder)
+constexpr int kDecodeMaxWarps = 12;               // streaming warps per CTA (plus a merger, a feeder and the finishers)
 constexpr int kDecodeQueue = 8;                   // task queue entries per CTA
 constexpr int kDecodeAhead = 12;                  // published pages a CTA keeps unclaimed
 constexpr int kDecodeFinish = 4;                  // split tasks in flight from the merger to the finishers
