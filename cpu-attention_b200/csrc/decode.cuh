@@ -64,7 +64,7 @@ constexpr int kDecodeQueue = 8;                   // task queue entries per CTA
 constexpr int kDecodeAhead = 12;                  // published pages a CTA keeps unclaimed
 constexpr int kDecodeFinish = 4;                  // split tasks in flight from the merger to the finishers
 constexpr int kDecodeFinishers = 2;               // finisher warps (entry f goes to finisher f % 2)
-constexpr int kDecodePageSlots = 32;              // page states in flight to the merger
+constexpr int kDecodePageSlots = 24;              // page states in flight to the merger
 constexpr int kDecodeBlkRing = 512;               // staged block ids per CTA (a ring over the page stream)
 constexpr int kDecodeBlkTask = 256;               // tasks up to this many pages stage their block ids
 
