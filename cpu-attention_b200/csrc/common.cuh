@@ -74,6 +74,13 @@ __device__ __forceinline__ void fence_barrier_init() {
 
 // Orders this thread's generic-proxy shared-memory accesses before later
 // async-proxy (bulk copy) accesses.
+// atomicAdd with acquire-release semantics at GPU scope.
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
 // Release/acquire fence at GPU scope (lighter than __threadfence's fence.sc).
 __device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 

@@ -615,14 +615,16 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
         slot[0] = M;
         slot[1] = L;
       }
-      fence_acq_rel_gpu();  // the partial before the ticket (release)
+      // the ticket is an acquire-release atomic: it releases the partial (every
+      // lane's writes, ordered before it by the warp barrier) and, for the
+      // last task, acquires the other tasks' partials
       __syncwarp();
       int ticket = 0;
       int* tk = p.tickets + (long long)ei * p.H + eh;
-      if (lane == 0) ticket = atomicAdd(tk, 1);
+      if (lane == 0) ticket = atom_add_acq_rel_gpu(tk, 1);
       ticket = __shfl_sync(0xffffffffu, ticket, 0);
       if (ticket != entask - 1) continue;
-      fence_acq_rel_gpu();  // the other tasks' partials after their tickets (acquire)
+      __syncwarp();
       const float* first = p.partial + (eslot - ej) * (E + 2);
       float MM = -INFINITY;
       for (int jj = lane; jj < entask; jj += 32) MM = fmaxf(MM, __ldcg(first + (long long)jj * (E + 2)));
