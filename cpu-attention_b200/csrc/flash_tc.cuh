@@ -254,8 +254,7 @@ __global__ void __launch_bounds__(384, 1) flash_tc_kernel(const __grid_constant_
           tc::mma_ss(tmem + C::T_S(x), tc::smem_desc(qaddr + off, 16, 8 * C::SWB, C::SWZ),
                      tc::smem_desc(kaddr + off, 16, 8 * C::SWB, C::SWZ), idS, kk > 0 ? 1u : 0u);
         }
-        tc::commit(&bars->s[x]);
-        if (x == 1 || j >= nt1) tc::commit(&bars->ke[ks]);
+        tc::commit(&bars->s[x]);  // (the softmax that sees it also frees K_j / V_{j-1})
         return true;
       };
       // O_x += P_x(j) V_j; the last user of V_j releases its slot
@@ -271,7 +270,6 @@ __global__ void __launch_bounds__(384, 1) flash_tc_kernel(const __grid_constant_
                      tc::smem_desc(vaddr + kk * 16 * C::SWB, C::CH_BYTES, 8 * C::SWB, C::SWZ), idO,
                      (j > 0 || kk > 0) ? 1u : 0u);
         tc::commit(&bars->pv[x]);
-        if (x == 1 || j >= nt1) tc::commit(&bars->ve[vs]);
         return true;
       };
       if (ok && nt0 > 0) ok = issue_s(0, 0);
@@ -310,6 +308,14 @@ __global__ void __launch_bounds__(384, 1) flash_tc_kernel(const __grid_constant_
         break;
       }
       tc::fence_after_sync();
+      // S_x(j) has completed, and with it every MMA issued before it: when this
+      // tile is the last user of K_j (tile B, or A where B has no tile j), and
+      // of V_{j-1}, those ring slots are free again. Arriving here instead of
+      // committing from the MMA thread keeps the MMA issuer on MMAs.
+      if (grp == 0 && lane == 0) {
+        if (x == (j < nt1 ? 1 : 0)) mbar_arrive(&bars->ke[j % C::KST]);
+        if (j >= 1 && x == (j - 1 < nt1 ? 1 : 0)) mbar_arrive(&bars->ve[(j - 1) % C::VST]);
+      }
       // the whole S row in registers: one TMEM round trip per tile
       uint32_t sr[C::BN];
 #pragma unroll
