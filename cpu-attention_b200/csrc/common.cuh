@@ -47,7 +47,20 @@ __device__ __forceinline__ long long warp_sum_ll(long long x) {
   for (int o = 16; o; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
   return x;
 }
+__device__ __forceinline__ int warp_sum_i(int x) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  return x;
+}
 // inclusive prefix sum over the warp
+__device__ __forceinline__ int warp_scan_i(int x, int lane) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  return x;
+}
 __device__ __forceinline__ long long warp_scan_ll(long long x, int lane) {
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {

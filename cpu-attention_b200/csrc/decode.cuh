@@ -35,7 +35,7 @@
 //         (cp.async.bulk, the TMA engine; L2 evict-first) into the warp's own
 //         ring of stages, completing on one mbarrier per stage. The warp
 //         computes the page's (m, l, acc) and deposits it in the page's slot
-//         of a 32-slot ring.
+//         of a 24-slot ring.
 //       - the merger folds the page states of each task in page order, then
 //         writes the output row, or hands a split task's state on.
 //       - the finishers write a split task's partial (m, l, acc) to the
@@ -67,6 +67,8 @@ constexpr int kDecodeFinishers = 2;               // finisher warps (entry f goe
 constexpr int kDecodePageSlots = 24;              // page states in flight to the merger
 constexpr int kDecodeBlkRing = 512;               // staged block ids per CTA (a ring over the page stream)
 constexpr int kDecodeBlkTask = 256;               // tasks up to this many pages stage their block ids
+constexpr int kSpinSleepNs = 32;                  // sleep between polls of a spinning warp
+constexpr int kPlanRegs = 4;                      // plan: page counts of 32 sequences per register kept
 
 struct DecodeParams {
   const void* q;
@@ -113,7 +115,7 @@ __device__ __forceinline__ int seq_pages(const DecodeParams& p, int i, int* len_
   }
   if (L < 0) L = 0;
   *len_out = (int)L;
-  return (int)((L + p.page - 1) / p.page);
+  return (int)(((unsigned)L + (unsigned)p.page - 1u) / (unsigned)p.page);  // L < 2^31: no wrap
 }
 
 // Tasks of an item of np pages.
@@ -141,10 +143,10 @@ struct Task {
 // Maps task ids, which only grow per walker, to tasks with a forward scan over
 // the sequences, 32 at a time (warp-collective).
 struct TaskWalk {
-  int ci0 = 0;          // first of the 32 sequences the scan starts at
-  long long tbase = 0;  // first task id of sequence ci0
-  long long sbase = 0;  // first partial slot of sequence ci0
-  __device__ __forceinline__ Task locate(const DecodeParams& p, const TaskPlan& plan, long long tid, int lane) {
+  int ci0 = 0;    // first of the 32 sequences the scan starts at
+  int tbase = 0;  // first task id of sequence ci0
+  int sbase = 0;  // first partial slot of sequence ci0
+  __device__ __forceinline__ Task locate(const DecodeParams& p, const TaskPlan& plan, int tid, int lane) {
     Task t;
     for (int i0 = ci0;; i0 += 32) {
       const int i = i0 + lane;
@@ -154,9 +156,9 @@ struct TaskWalk {
         np = seq_pages(p, i, &L);
         nt = item_tasks(np, plan.size(i));
       }
-      const long long tk = (long long)nt * p.H, sl = nt > 1 ? tk : 0;
-      const long long tincl = warp_scan_ll(tk, lane) + tbase;
-      const long long sincl = warp_scan_ll(sl, lane) + sbase;
+      const int tk = nt * p.H, sl = nt > 1 ? tk : 0;
+      const int tincl = warp_scan_i(tk, lane) + tbase;
+      const int sincl = warp_scan_i(sl, lane) + sbase;
       const unsigned hit = __ballot_sync(0xffffffffu, i < p.B && tincl > tid);
       if (hit) {
         const int src = __ffs(hit) - 1;
@@ -165,9 +167,9 @@ struct TaskWalk {
         t.len = __shfl_sync(0xffffffffu, L, src);
         t.raw = __shfl_sync(0xffffffffu, raw, src);
         t.ntask = __shfl_sync(0xffffffffu, nt, src);
-        const long long t0 = __shfl_sync(0xffffffffu, tincl - tk, src);
-        const long long s0 = __shfl_sync(0xffffffffu, sincl - sl, src);
-        const int off = (int)(tid - t0);
+        const int t0 = __shfl_sync(0xffffffffu, tincl - tk, src);
+        const int s0 = __shfl_sync(0xffffffffu, sincl - sl, src);
+        const int off = tid - t0;
         t.h = off / t.ntask;
         t.j = off - t.h * t.ntask;
         t.pg0 = (int)((long long)t.j * t.np / t.ntask);  // even split of the item's pages
@@ -250,7 +252,7 @@ __device__ __forceinline__ bool spin_until(F ok, volatile int* abort) {
   for (uint32_t it = 1;; ++it) {
     if (ok()) return true;
     if ((it & 63u) == 0 && (*abort || global_timer_ns() - t0 > kWaitLimitNs)) return false;
-    __nanosleep(32);
+    __nanosleep(kSpinSleepNs);
   }
 }
 
@@ -281,55 +283,6 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
   float* sPage = sFinO + FQ * E;                              // [R][E + 4]: acc[E], m, l
   int* sBlk = reinterpret_cast<int*>(sPage + R * (E + 4));   // [RB]: block id of stream page g at g % RB
 
-  // ---- plan: task sizes and the number of tasks (every warp alike)
-  long long NP = 0, NT = 0;
-  for (int i0 = 0; i0 < p.B; i0 += 32) {
-    const int i = i0 + lane;
-    if (i < p.B) {
-      int L;
-      NP += seq_pages(p, i, &L);
-    }
-  }
-  NP = warp_sum_ll(NP) * p.H;
-  TaskPlan plan;
-  plan.Ub = W * p.pages_per_warp;
-  if (NP > (long long)p.task_cap * plan.Ub) plan.Ub = (int)((NP + p.task_cap - 1) / p.task_cap);
-  plan.Us = max(W, plan.Ub / p.tail_div);
-  plan.icut = p.B;
-  if (plan.Us < plan.Ub) {
-    // the first sequence from which on at most an eighth of the pages remain
-    const long long need = NP - NP / 8;
-    long long base = 0;
-    for (int i0 = 0; i0 < p.B && plan.icut == p.B; i0 += 32) {
-      const int i = i0 + lane;
-      int L = 0;
-      const long long pg = i < p.B ? (long long)seq_pages(p, i, &L) * p.H : 0;
-      const long long before = warp_scan_ll(pg, lane) - pg + base;
-      const unsigned hit = __ballot_sync(0xffffffffu, i < p.B && before >= need);
-      if (hit) {
-        const int src = __ffs(hit) - 1;
-        plan.icut = i0 + src;
-        base = __shfl_sync(0xffffffffu, before, src);
-      } else {
-        base = __shfl_sync(0xffffffffu, before + pg, 31);
-      }
-    }
-    const long long tail = NP - base;  // pages of the small tasks (base: pages before icut)
-    // only when every CTA gets a small task or more, and the split tasks keep
-    // within the partial slots (at most 2 np / U slots per split item)
-    if (plan.icut == p.B || tail < (long long)gridDim.x * plan.Us ||
-        2 * tail / plan.Us + 2 * NP / plan.Ub > 2LL * p.task_cap)
-      plan.icut = p.B;
-  }
-  for (int i0 = 0; i0 < p.B; i0 += 32) {
-    const int i = i0 + lane;
-    if (i < p.B) {
-      int L;
-      NT += item_tasks(seq_pages(p, i, &L), plan.size(i));
-    }
-  }
-  NT = warp_sum_ll(NT) * p.H;
-
   uint8_t* wbase = smem_raw + (size_t)w * p.warp_bytes;
   float* sP = reinterpret_cast<float*>(wbase + (size_t)p.stages * p.stage_bytes);
   int4* sTag = reinterpret_cast<int4*>(sP + kDecodeMaxPage);  // per stage: task position, page, stream page
@@ -346,6 +299,72 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
 
   if (w == W + 1) {
     // ================================================================= feeder
+    // ---- plan: task sizes and the number of tasks (only the feeder needs
+    // them; the other warps go straight to their roles). The pages of the
+    // first kPlanRegs * 32 sequences are read once and kept in registers for
+    // the later passes.
+    constexpr int PR = kPlanRegs;
+    int npr[PR];
+    int NP1 = 0, NT1 = 0;  // per head: pages, tasks (the totals are H times these)
+    for (int i0 = 0, k = 0; i0 < p.B; i0 += 32, ++k) {
+      const int i = i0 + lane;
+      int L, np = 0;
+      if (i < p.B) np = seq_pages(p, i, &L);
+      NP1 += np;
+#pragma unroll
+      for (int kk = 0; kk < PR; ++kk)
+        if (kk == k) npr[kk] = np;
+    }
+    auto pages_of = [&](int i0, int k) -> int {  // sequence i0 + lane's pages
+      int np = 0;
+#pragma unroll
+      for (int kk = 0; kk < PR; ++kk)
+        if (kk == k) np = npr[kk];
+      if (k >= PR && i0 + lane < p.B) {
+        int L;
+        np = seq_pages(p, i0 + lane, &L);
+      }
+      return np;
+    };
+    const long long NP = (long long)warp_sum_i(NP1) * p.H;
+    TaskPlan plan;
+    plan.Ub = W * p.pages_per_warp;
+    if (NP > (long long)p.task_cap * plan.Ub) plan.Ub = (int)((NP + p.task_cap - 1) / p.task_cap);
+    plan.Us = max(W, plan.Ub / p.tail_div);
+    plan.icut = p.B;
+    if (plan.Us < plan.Ub) {
+      // the first sequence from which on at most an eighth of the pages remain
+      // (in pages per head: every head of a sequence has the same pages)
+      const long long NPh = NP / p.H;
+      const int need = (int)(NPh - NPh / 8);
+      int base = 0;
+      for (int i0 = 0, k = 0; i0 < p.B && plan.icut == p.B; i0 += 32, ++k) {
+        const int i = i0 + lane;
+        const int pg = pages_of(i0, k);
+        const int before = warp_scan_i(pg, lane) - pg + base;
+        const unsigned hit = __ballot_sync(0xffffffffu, i < p.B && before >= need);
+        if (hit) {
+          const int src = __ffs(hit) - 1;
+          plan.icut = i0 + src;
+          base = __shfl_sync(0xffffffffu, before, src);
+        } else {
+          base = __shfl_sync(0xffffffffu, before + pg, 31);
+        }
+      }
+      const long long tail = NP - (long long)base * p.H;  // pages of the small tasks
+      // only when every CTA gets a small task or more, and the split tasks keep
+      // within the partial slots (at most 2 np / U slots per split item)
+      if (plan.icut == p.B || tail < (long long)gridDim.x * plan.Us ||
+          2 * tail / plan.Us + 2 * NP / plan.Ub > 2LL * p.task_cap)
+        plan.icut = p.B;
+    }
+    for (int i0 = 0, k = 0; i0 < p.B; i0 += 32, ++k) {
+      const int i = i0 + lane;
+      const int np = pages_of(i0, k);
+      if (i < p.B) NT1 += item_tasks(np, plan.size(i));
+    }
+    const int NT = warp_sum_i(NT1) * p.H;
+
     // Keeps one task staged (grabbed, located, its query row in registers)
     // and publishes it while fewer than p.ahead published pages are unclaimed
     // and a queue entry is free (merged); then stages the next, so the grab's
