@@ -136,7 +136,9 @@ class Decode:
             attended = [int(n) + extra for n in lens]
         self.kv_bytes = sum(attended) * H * E * dtype.itemsize * 2
         self.attend_lens = torch.tensor(attended, dtype=torch.int32, device=dev)
-        self.launches_per_step = 2 if (append or engine) else 1
+        # engine: store + decode; a one-token append is fused into the decode
+        self.launches_per_step = 2 if engine else 1
+        self.counts = [b - a for a, b in shard_ranges(lens_all, world)] if engine else [B] * world
 
     # the measured step (device-resident inputs)
     def step(self):
@@ -145,9 +147,16 @@ class Decode:
             K = self.K
             K.module().decode(K.runtime(), self.q[:, 0], self.kc, self.vc, None, None, None, self.eng_lens, self.bt,
                               None, self.out)
-            return
-        self.C.flash_attn_with_kvcache(self.q, self.kc, self.vc, k=self.kn, v=self.vn, cache_seqlens=self.lens,
-                                       page_table=self.bt)
+            return self.out
+        return self.C.flash_attn_with_kvcache(self.q, self.kc, self.vc, k=self.kn, v=self.vn, cache_seqlens=self.lens,
+                                              page_table=self.bt)
+
+    # the step followed by the optional collective: every rank's outputs
+    # all-gathered in sequence order (NCCL all_gather_into_tensor)
+    def gather_step(self):
+        from cpu_attention.shard import gather_outputs
+        out = self.step()
+        return gather_outputs(out.reshape(out.shape[0], -1), self.counts)
 
     # the dominant kernel alone: decode over the attended lengths, no store
     def kernel_step(self):
@@ -371,7 +380,7 @@ class ClockSampler:
 # capture of the same command (the files under profiles/ give the commands).
 TRAFFIC = {
     "cfg2": (283.1e6, "profiles/decode_kernel_cfg2.md"),
-    "cfg4": (251.1e6, "profiles/flash_tc_kernel_cfg4.md"),
+    "cfg4": (249.2e6, "profiles/flash_tc_kernel_cfg4.md"),
 }
 
 HOST_HIDE_CYCLES = 400_000  # ~0.2 ms of device spin: longer than the host needs to enqueue one step
@@ -554,6 +563,14 @@ def main():
     e2e_ms = timed(wl.e2e_step, args.steps, 2, flush, stream, hide_host=False)
     e2e_total = max_over_ranks(sum(e2e_ms), world)
     e2e_value = units / (e2e_total / args.steps * 1e-3) / scale
+
+    # N > 1 decode: the same step with the output all-gather after it
+    with_gather = None
+    if world > 1 and hasattr(wl, "gather_step"):
+        g_ms = timed(wl.gather_step, args.steps, 2, flush, stream)
+        g_total = max_over_ranks(sum(g_ms), world)
+        with_gather = {"value": round(units / (g_total / args.steps * 1e-3) / scale, 3), "unit": unit,
+                       "ms_per_step": round(g_total / args.steps, 4), "collective": "all_gather_into_tensor"}
     barrier(world)
     clocks = sampler.stop() if sampler else None
 
@@ -565,6 +582,8 @@ def main():
             "e2e": {"value": round(e2e_value, 3), "unit": unit, "h2d_bytes_per_step": wl.h2d_bytes,
                     "d2h_bytes_per_step": wl.d2h_bytes, "ms_per_step": round(e2e_total / args.steps, 4)},
             "gpu_launches": wl.launches_per_step * args.steps, "clocks": clocks}
+    if with_gather is not None:
+        line["with_gather"] = with_gather
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
         sec, cunits, n = cpu_baseline(wl, threads)
