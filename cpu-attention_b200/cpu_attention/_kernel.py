@@ -39,6 +39,8 @@ SIGNATURES = {
     "ca_decode_workspace_bytes": (_SZ, [_I64, _I64, _I64, _I64, _I32, _I32]),
     "ca_decode": (_I32, [_P, _I64, _P, _P, _I64, _P, _P, _I64, _P, _P, _P, _I64, _P,
                          _I64, _I64, _I64, _I64, _I32, _F, _P, _SZ, _P]),
+    "ca_decode_append": (_I32, [_P, _I64, _P, _P, _I64, _P, _P, _I64, _I64, _I64, _P, _P, _I64, _P,
+                                _I64, _I64, _I64, _I64, _I32, _F, _P, _SZ, _P]),
     "ca_decode_noalloc": (_I32, [_P, _I64, _P, _P, _I64, _P, _P, _I64, _P, _P, _P, _I64, _P,
                                  _I64, _I64, _I64, _I64, _I32, _F, _P]),
     "ca_flash": (_I32, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _PI64, _PI64, _PI64, _F, _I32, _I32, _P,

@@ -60,9 +60,10 @@ def _scale(scale):
 def decode(rt, q, k_cache, v_cache, k, v, slots, lens, page_table, scale, dst):
     """Paged decode of q ``[seqs, (1,) heads, dim]`` (MHA). With k/v, each
     sequence's new token is stored first: at ``slots`` (then ``lens`` is the
-    length after the store), or appended at ``lens`` (the length before). Writes
-    ``dst`` when given, else a new tensor; returns it, or None
-    (`_C.mojo:87-171`)."""
+    length after the store), or appended at ``lens`` (the length before). k/v
+    of shape ``[seqs, n, heads, dim]`` with n > 1 append n tokens at ``lens``
+    in the same launch (``ca_decode_append``). Writes ``dst`` when given, else a
+    new tensor; returns it, or None (`_C.mojo:87-171`)."""
     del rt
     dev = _cuda(q, k_cache, v_cache, k, v, slots, lens, page_table, dst)
     if dev is None or not isinstance(q, torch.Tensor):
@@ -83,11 +84,16 @@ def decode(rt, q, k_cache, v_cache, k, v, slots, lens, page_table, scale, dst):
     if not _int_vector(lens, torch.int32, b):
         return None
     store = k is not None
+    n_new = 1
     if store:
-        if v is None or k.shape != q.shape or v.shape != q.shape or v.stride() != k.stride():
+        multi = (nd == 4 and slots is None and k.dim() == 4 and k.shape[0] == b and k.shape[1] > 1
+                 and tuple(k.shape[2:]) == (heads, hd))
+        if v is None or (k.shape != q.shape and not multi) or v.shape != k.shape or v.stride() != k.stride():
             return None
         if k.dtype != q.dtype or v.dtype != q.dtype or not _rows_ok(k, hd):
             return None
+        if multi:
+            n_new = k.shape[1]
     elif v is not None:
         return None
     if slots is not None and not (store and _int_vector(slots, torch.int64, b)):
@@ -107,12 +113,19 @@ def decode(rt, q, k_cache, v_cache, k, v, slots, lens, page_table, scale, dst):
         return None
     ws = K.workspace(dev, stream, need)
     with K.on_device(dev):
-        rc = lib.ca_decode(
-            q.data_ptr(), q.stride(0), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.shape[0],
-            k.data_ptr() if store else None, v.data_ptr() if store else None, k.stride(0) if store else 0,
-            slots.data_ptr() if slots is not None else None, lens.data_ptr(), page_table.data_ptr(),
-            page_table.shape[1], out.data_ptr(), b, heads, hd, page, dt, _scale(scale), ws.data_ptr(),
-            ws.numel(), stream)
+        if n_new > 1:
+            rc = lib.ca_decode_append(
+                q.data_ptr(), q.stride(0), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.shape[0],
+                k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1), n_new, lens.data_ptr(),
+                page_table.data_ptr(), page_table.shape[1], out.data_ptr(), b, heads, hd, page, dt,
+                _scale(scale), ws.data_ptr(), ws.numel(), stream)
+        else:
+            rc = lib.ca_decode(
+                q.data_ptr(), q.stride(0), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.shape[0],
+                k.data_ptr() if store else None, v.data_ptr() if store else None, k.stride(0) if store else 0,
+                slots.data_ptr() if slots is not None else None, lens.data_ptr(), page_table.data_ptr(),
+                page_table.shape[1], out.data_ptr(), b, heads, hd, page, dt, _scale(scale), ws.data_ptr(),
+                ws.numel(), stream)
     if not _check_rc(rc):
         return None
     if K.CHECK:

@@ -110,8 +110,14 @@ def flash_attn_with_kvcache(
             raise ValueError("cpu_attention: `cache_seqlens` is required")
         cache_seqlens = torch.full((q.shape[0],), cache_seqlens, dtype=torch.int32, device=q.device)
     if k is not None and k.shape[1] != 1:
-        # Several new tokens (a prompt): store them at cache_seqlens + j, then
-        # decode over the grown cache (`flash_attn_interface.py:141-149`).
+        # Several new tokens (a prompt): appended at cache_seqlens + j by the
+        # decode launch itself; when that is declined, the reference's two
+        # steps (`flash_attn_interface.py:109-117`): store them at
+        # cache_seqlens + j, then decode over the grown cache.
+        if cache_seqlens.device == k_cache.device and page_table.device == k_cache.device:
+            out = _native.decode(0, q, k_cache, v_cache, k, v, None, cache_seqlens, page_table, softmax_scale, None)
+            if out is not None:
+                return out
         n, page = k.shape[1], k_cache.shape[2]
         dev = k_cache.device
         lens = cache_seqlens.to(dev)

@@ -217,11 +217,18 @@ size_t ca_decode_workspace_bytes(int64_t batch, int64_t heads, int64_t head_dim,
   return decode_ws_bytes(batch, heads, dev);
 }
 
-int ca_decode(const void* q, int64_t q_stride, void* k_cache, void* v_cache, int64_t num_blocks,
-              const void* k_new, const void* v_new, int64_t kv_stride, const int64_t* slots, const int32_t* lens,
-              const int32_t* page_table, int64_t table_width, void* out, int64_t batch, int64_t heads,
-              int64_t head_dim, int64_t page, int dtype, float softmax_scale, void* workspace,
-              size_t workspace_bytes, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// ca_decode and ca_decode_append: n_new tokens per sequence (k_new rows
+// kv_stride apart between sequences, kv_tstride between tokens), stored by
+// slot (n_new == 1 only) or appended at lens[i].
+int decode_impl(const void* q, int64_t q_stride, void* k_cache, void* v_cache, int64_t num_blocks,
+                const void* k_new, const void* v_new, int64_t kv_stride, int64_t kv_tstride, int64_t n_new,
+                const int64_t* slots, const int32_t* lens, const int32_t* page_table, int64_t table_width,
+                void* out, int64_t batch, int64_t heads, int64_t head_dim, int64_t page, int dtype,
+                float softmax_scale, void* workspace, size_t workspace_bytes, void* stream) {
   if (dtype != CA_DTYPE_F32 && dtype != CA_DTYPE_BF16) return CA_EDTYPE;
   if (!head_dim_ok(head_dim)) return CA_EHEADDIM;
   if (!page_ok(page)) return CA_EPAGE;
@@ -232,6 +239,8 @@ int ca_decode(const void* q, int64_t q_stride, void* k_cache, void* v_cache, int
   if (!q || !k_cache || !v_cache || !lens || !page_table || !out || !workspace) return CA_ENULL;
   if (q_stride < heads * head_dim) return CA_ELAYOUT;
   if (k_new && kv_stride < heads * head_dim) return CA_ELAYOUT;
+  if (k_new && n_new > 1 && (kv_tstride < heads * head_dim || kv_stride < n_new * kv_tstride)) return CA_ELAYOUT;
+  if (n_new < 0 || n_new > (1 << 20) || (slots && n_new != 1)) return CA_ESHAPE;
   // whole pages move by 16-byte bulk copies
   if (!aligned(k_cache, 16) || !aligned(v_cache, 16)) return CA_ELAYOUT;
   const size_t es = elem_size(dtype);
@@ -282,10 +291,11 @@ int ca_decode(const void* q, int64_t q_stride, void* k_cache, void* v_cache, int
   prm.vc = v_cache;
   prm.num_blocks = num_blocks;
   prm.lens = lens;
-  prm.extra = (k_new && !slots) ? 1 : 0;
+  prm.extra = (k_new && !slots) ? (int)n_new : 0;
   prm.k_new = prm.extra ? k_new : nullptr;
   prm.v_new = prm.extra ? v_new : nullptr;
   prm.kv_stride = kv_stride;
+  prm.kv_tstride = kv_tstride;
   prm.counter = counter;
   prm.page_table = page_table;
   prm.pt_stride = table_width;
@@ -311,6 +321,31 @@ int ca_decode(const void* q, int64_t q_stride, void* k_cache, void* v_cache, int
   prm.status = status;
   if (dtype == CA_DTYPE_BF16) return dispatch_decode<__nv_bfloat16>(head_dim, prm, pl, s, device);
   return dispatch_decode<float>(head_dim, prm, pl, s, device);
+}
+
+}  // namespace
+
+extern "C" {
+
+int ca_decode(const void* q, int64_t q_stride, void* k_cache, void* v_cache, int64_t num_blocks,
+              const void* k_new, const void* v_new, int64_t kv_stride, const int64_t* slots, const int32_t* lens,
+              const int32_t* page_table, int64_t table_width, void* out, int64_t batch, int64_t heads,
+              int64_t head_dim, int64_t page, int dtype, float softmax_scale, void* workspace,
+              size_t workspace_bytes, void* stream) {
+  return decode_impl(q, q_stride, k_cache, v_cache, num_blocks, k_new, v_new, kv_stride, 0, k_new ? 1 : 0, slots,
+                     lens, page_table, table_width, out, batch, heads, head_dim, page, dtype, softmax_scale,
+                     workspace, workspace_bytes, stream);
+}
+
+int ca_decode_append(const void* q, int64_t q_stride, void* k_cache, void* v_cache, int64_t num_blocks,
+                     const void* k_new, const void* v_new, int64_t kv_stride, int64_t kv_token_stride,
+                     int64_t n_new, const int32_t* lens, const int32_t* page_table, int64_t table_width, void* out,
+                     int64_t batch, int64_t heads, int64_t head_dim, int64_t page, int dtype, float softmax_scale,
+                     void* workspace, size_t workspace_bytes, void* stream) {
+  if (n_new < 1 || !k_new || !v_new) return CA_ESHAPE;
+  return decode_impl(q, q_stride, k_cache, v_cache, num_blocks, k_new, v_new, kv_stride, kv_token_stride, n_new,
+                     nullptr, lens, page_table, table_width, out, batch, heads, head_dim, page, dtype,
+                     softmax_scale, workspace, workspace_bytes, stream);
 }
 
 int ca_flash(const void* q, const void* k, const void* v, void* out, int64_t batch, int64_t seq_q, int64_t seq_k,

@@ -46,10 +46,11 @@
 //     the fp32 query as broadcast loads; P.V: lanes own 4 dims of a V row.
 //   * Masked keys never reach P.V (the loop stops at the last valid key), so
 //     NaN in unused slots of a page cannot leak (`paged_attn.mojo:686-687`).
-//   * A one-token append through the page table is fused: the warp that
-//     streams the new token's page patches the token into shared memory after
-//     the copy lands and writes it to the cache (it is that page's only reader
-//     in the call), so no second launch is needed.
+//   * An append through the page table (one token, or several: a prompt) is
+//     fused: the warp that streams a page holding new tokens patches them
+//     into shared memory after the copy lands and writes them to the cache
+//     (it is that page's only reader in the call), so no second launch is
+//     needed.
 #pragma once
 
 #include "common.cuh"
@@ -77,10 +78,11 @@ struct DecodeParams {
   const void* vc;
   long long num_blocks;
   const int* lens;
-  int extra;            // 1: the call appends a token at lens[i] (fused)
-  const void* k_new;    // the appended token's K/V rows (extra == 1)
+  int extra;             // tokens the call appends at lens[i] (fused; 0: none)
+  const void* k_new;     // the appended tokens' K/V rows (extra > 0)
   const void* v_new;
-  long long kv_stride;  // elements between sequences of k_new/v_new
+  long long kv_stride;   // elements between sequences of k_new/v_new
+  long long kv_tstride;  // elements between the tokens of one sequence (extra > 1)
   const int* page_table;
   long long pt_stride;  // table width W
   void* out;
@@ -215,7 +217,8 @@ struct QueueEntry {
   int n;           // pages of the task
   int start;       // the task's first page in the CTA's page stream
   int len;         // attended length of sequence i
-  int apg;         // page holding the appended token, -1: none in this task
+  int raw;         // cache_seqlens[i]: the appended tokens sit at [raw, raw + extra)
+  int apg0, apg1;  // this task's pages holding appended tokens ([apg0, apg1]; apg0 > apg1: none)
   int staged;      // 1: its block ids are in the CTA's block-id ring
   long long slot;  // partial slot (ntask > 1)
 };
@@ -374,7 +377,7 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
     const T* qbase = static_cast<const T*>(p.q);
     constexpr int QR = (E + 31) / 32;
     constexpr int BR = kDecodeBlkTask / 32;
-    int sid = -1, sapg = -1;  // staged task id (-1: the failing grab), appended page
+    int sid = -1, sapg0 = 0, sapg1 = -1;  // staged task id (-1: the failing grab), its appended pages
     Task st;
     T qraw[QR];
     int sblk[BR];  // the task's block ids (tasks of at most kDecodeBlkTask pages)
@@ -402,10 +405,11 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
 #pragma unroll
       for (int k = 0; k < QR; ++k)
         if (lane + 32 * k < E) qraw[k] = qr[lane + 32 * k];
-      sapg = -1;
-      if (p.extra && st.len == st.raw + 1) {
-        const int apg = (st.len - 1) / p.page;
-        if (apg >= st.pg0 && apg < st.pg1) sapg = apg;
+      sapg0 = 0;
+      sapg1 = -1;
+      if (p.extra > 0 && st.len == st.raw + p.extra) {  // (a clamped length appends nothing)
+        sapg0 = max(st.raw / p.page, st.pg0);
+        sapg1 = min((st.len - 1) / p.page, st.pg1 - 1);
       }
       const int n = st.pg1 - st.pg0;
       if (n <= kDecodeBlkTask) {
@@ -483,7 +487,9 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
           e->n = st.pg1 - st.pg0;
           e->start = published;
           e->len = st.len;
-          e->apg = sapg;
+          e->raw = st.raw;
+          e->apg0 = sapg0;
+          e->apg1 = sapg1;
           e->staged = fast ? 1 : 0;
           e->slot = st.slot;
         }
@@ -757,8 +763,8 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
   unsigned fail_idx = 0;  // the first page not waited for
   int cur = -1;           // task position whose fields are loaded
   struct {
-    int i, h, len, apg;
-  } t = {0, 0, 0, -1};
+    int i, h, len, raw, apg0, apg1;
+  } t = {0, 0, 0, 0, 0, -1};
   const float* sQ = sRows;
   for (;;) {
     produce();
@@ -782,7 +788,9 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
       t.i = sQe[r].i;
       t.h = sQe[r].h;
       t.len = sQe[r].len;
-      t.apg = sQe[r].apg;
+      t.raw = sQe[r].raw;
+      t.apg0 = sQe[r].apg0;
+      t.apg1 = sQe[r].apg1;
       sQ = sRows + r * E;
     }
     const float4* sQ4 = reinterpret_cast<const float4*>(sQ);
@@ -798,33 +806,35 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
       uint8_t* stage = wbase + (size_t)s * p.stage_bytes;
       const int pg = tag.y;
       const int ntok = min(p.page, t.len - pg * p.page);
-      if (pg == t.apg) {
-        // the appended token: into the staged page (shared) and the cache
-        // (global), K transposed as the page layout wants, V as a row
-        const int tt = (t.len - 1) - pg * p.page;
-        const T* kn = static_cast<const T*>(p.k_new) + (long long)t.i * p.kv_stride + (long long)t.h * E;
-        const T* vn = static_cast<const T*>(p.v_new) + (long long)t.i * p.kv_stride + (long long)t.h * E;
+      if (pg >= t.apg0 && pg <= t.apg1) {
+        // appended tokens in this page: into the staged page (shared) and the
+        // cache (global), K transposed as the page layout wants, V as rows.
+        // A page is streamed by exactly one warp in a call, so each token is
+        // written once.
+        const int lo = max(t.raw - pg * p.page, 0), hi = min(t.raw + p.extra - pg * p.page, p.page);
         int gblk = __ldg(p.page_table + (long long)t.i * p.pt_stride + pg);
         if (gblk < 0 || gblk >= p.num_blocks) gblk = -1;
         T* sKe = reinterpret_cast<T*>(stage);
-        T* sVt = reinterpret_cast<T*>(stage + p.kslot_bytes) + (size_t)tt * E;
+        T* sV = reinterpret_cast<T*>(stage + p.kslot_bytes);
         const long long pbase = gblk >= 0 ? ((long long)gblk * p.H + t.h) * (long long)p.page * E : 0;
         T* gK = static_cast<T*>(const_cast<void*>(p.kc)) + pbase;
-        T* gV = static_cast<T*>(const_cast<void*>(p.vc)) + pbase + (long long)tt * E;
-        for (int d = lane; d < E; d += 32) {
-          const T kv = kn[d], vv = vn[d];
+        T* gV = static_cast<T*>(const_cast<void*>(p.vc)) + pbase;
+        const long long rowbase = (long long)t.i * p.kv_stride + (long long)t.h * E;
+        for (int idx = lane; idx < (hi - lo) * E; idx += 32) {
+          const int tt = lo + idx / E, d = idx % E;
+          const long long src = rowbase + (long long)(pg * p.page + tt - t.raw) * p.kv_tstride + d;
+          const T kv = static_cast<const T*>(p.k_new)[src], vv = static_cast<const T*>(p.v_new)[src];
           const int ko = Tile::kBF ? (((d >> 1) * p.page + tt) * 2 + (d & 1)) : (d * p.page + tt);
           sKe[ko] = kv;
-          sVt[d] = vv;
+          sV[tt * E + d] = vv;
           if (gblk >= 0) {
             gK[ko] = kv;
-            gV[d] = vv;
+            gV[tt * E + d] = vv;
           }
         }
+        fence_proxy_async_smem();  // generic writes to a stage the copy engine refills later
         __syncwarp();
       }
-
-
 
       // ---- Q.K^T for the page's ntok keys
       const uint32_t* sK = reinterpret_cast<const uint32_t*>(stage);

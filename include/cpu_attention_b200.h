@@ -109,6 +109,27 @@ CA_API int ca_decode(const void* q, int64_t q_stride, void* k_cache, void* v_cac
               int dtype, float softmax_scale, void* workspace,
               size_t workspace_bytes, void* stream);
 
+/* ---- decode with a several-token append, in one launch ---------------------
+ * Replaces the reference's two-step path for k/v holding several new tokens
+ * per sequence (`flash_attn_interface.py:109-117`: the tokens are stored at
+ * cache_seqlens + j by `reshape_and_cache`, then `_C.decode` attends the grown
+ * cache), §8(f) rank 1 of the hot path: here the decode launch itself writes
+ * the tokens (the warp that streams a page holding new tokens patches them in
+ * and writes them to the cache) and attends lens[i] + n_new keys.
+ * k_new/v_new: token j of sequence i at element i * kv_stride +
+ *   j * kv_token_stride (+ head * head_dim + dim); kv_token_stride >=
+ *   heads * head_dim and kv_stride >= n_new * kv_token_stride.
+ * The other arguments are ca_decode's with slots = NULL. n_new = 1 is
+ * ca_decode's fused one-token append.
+ */
+CA_API int ca_decode_append(const void* q, int64_t q_stride, void* k_cache,
+              void* v_cache, int64_t num_blocks, const void* k_new,
+              const void* v_new, int64_t kv_stride, int64_t kv_token_stride,
+              int64_t n_new, const int32_t* lens, const int32_t* page_table,
+              int64_t table_width, void* out, int64_t batch, int64_t heads,
+              int64_t head_dim, int64_t page, int dtype, float softmax_scale,
+              void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- paged decode without allocation -----------------------------------
  * No counterpart in the reference: an addition for callers that cannot
  * allocate device memory (an engine that reserves all GPU memory up front and

@@ -94,6 +94,59 @@ def test_append_one_token(dtype):
     assert err <= tol
 
 
+def _prompt_case(lens, n, h, d, page, dtype, seed):
+    """Caches (NaN elsewhere) holding lens[i] tokens per sequence, with distinct
+    blocks for each sequence's pages up to lens[i] + n, and n new tokens."""
+    g = torch.Generator().manual_seed(seed)
+    npages = [-(-(ln + n) // page) for ln in lens]
+    order = torch.randperm(sum(npages), generator=g).to(torch.int32)
+    bt = torch.zeros(len(lens), max(npages), dtype=torch.int32)
+    start = 0
+    for i, npg in enumerate(npages):
+        bt[i, :npg] = order[start:start + npg]
+        start += npg
+    kc = torch.full((sum(npages), h, page, d), float("nan"), dtype=dtype, device=DEV)
+    vc = kc.clone()
+    C = _api()
+    ks, vs = [], []
+    for i, ln in enumerate(lens):
+        k, v = (torch.randn(ln, h, d, generator=g).to(dtype) for _ in range(2))
+        ks.append(k)
+        vs.append(v)
+        if ln:
+            pos = torch.arange(ln)
+            C.reshape_and_cache(k.to(DEV), v.to(DEV), kc, vc, (bt[i, pos // page].long() * page + pos % page).to(DEV))
+    q = torch.randn(len(lens), 1, h, d, generator=g).to(dtype)
+    # the new tokens as a strided view of a fused [B, n, 2, h, d] projection
+    kv = torch.randn(len(lens), n, 2, h, d, generator=g).to(dtype)
+    return q.to(DEV), kc, vc, bt.to(DEV), ks, vs, kv
+
+
+@pytest.mark.parametrize("dtype", cases.DTYPES)
+@pytest.mark.parametrize("page,n", [(16, 2), (16, 17), (32, 40), (16, 1)])
+def test_append_prompt_in_one_launch(dtype, page, n):
+    """Several new tokens per sequence (a prompt) are written at cache_seqlens + j
+    and attended by the decode launch itself (the reference stores them first,
+    `flash_attn_interface.py:109-117`): the output matches the float64 oracle
+    over the grown sequences, and the caches match, bit for bit, the ones the
+    reference's two steps (reshape_and_cache, then decode) leave."""
+    C = _api()
+    lens, h, d = [0, 5, 31, 64, 300], 4, 64
+    q, kc, vc, bt, ks, vs, kv = _prompt_case(lens, n, h, d, page, dtype, seed=7 + n)
+    kn, vn = kv[:, :, 0], kv[:, :, 1]
+    kc2, vc2 = kc.clone(), vc.clone()
+    seqlens = torch.tensor(lens, dtype=torch.int32, device=DEV)
+    out = C.flash_attn_with_kvcache(q, kc, vc, k=kn.to(DEV), v=vn.to(DEV), cache_seqlens=seqlens, page_table=bt)
+    ref = np.concatenate([F64.attention(q[i:i + 1], torch.cat([ks[i], kn[i]], 0)[None],
+                                        torch.cat([vs[i], vn[i]], 0)[None], d ** -0.5) for i in range(len(lens))])
+    err, tol = F64.check(out, ref, dtype == torch.bfloat16, paged=True)
+    assert err <= tol, err
+    pos = torch.tensor(lens)[:, None] + torch.arange(n)[None]
+    slots = bt.cpu().long().gather(1, pos // page) * page + pos % page
+    C.reshape_and_cache(kn.reshape(-1, h, d).to(DEV), vn.reshape(-1, h, d).to(DEV), kc2, vc2, slots.flatten().to(DEV))
+    assert np.array_equal(bits(kc), bits(kc2)) and np.array_equal(bits(vc), bits(vc2))
+
+
 @pytest.mark.parametrize("dtype", cases.DTYPES)
 def test_fused_projection_strides(dtype):
     """q and the new k/v as chunks of one fused [b, 1, 3 h d] projection
