@@ -85,8 +85,6 @@ __device__ __forceinline__ void fence_barrier_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
 
-// Orders this thread's generic-proxy shared-memory accesses before later
-// async-proxy (bulk copy) accesses.
 // atomicAdd with acquire-release semantics at GPU scope.
 __device__ __forceinline__ int atom_add_acq_rel_gpu(int* p, int v) {
   int old;
@@ -97,6 +95,8 @@ __device__ __forceinline__ int atom_add_acq_rel_gpu(int* p, int v) {
 // Release/acquire fence at GPU scope (lighter than __threadfence's fence.sc).
 __device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 
+// Orders this thread's generic-proxy shared-memory accesses before later
+// async-proxy (bulk copy, tensor core) accesses.
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

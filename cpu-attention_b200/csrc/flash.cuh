@@ -46,8 +46,17 @@ __global__ void __launch_bounds__(128) flash_generic_kernel(const __grid_constan
   float* sQ = sV + BK * E;       // [BQ][E]
   float* sP = sQ + BQ * E;       // [4 warps][BK][RW]  (key-major: 4 rows per float4)
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int b = blockIdx.z, h = blockIdx.y;
-  const int q0 = blockIdx.x * BQ;
+  // Causal: heaviest query blocks of every (batch, head) launch first (the
+  // linear block index maps to a descending query block, slowest).
+  int blk = (int)blockIdx.x, h = (int)blockIdx.y, b = (int)blockIdx.z;
+  if (p.causal) {
+    const int nhb = (int)(gridDim.y * gridDim.z);
+    const int lin = (int)(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z));
+    blk = (int)gridDim.x - 1 - lin / nhb;
+    h = (lin % nhb) % (int)gridDim.y;
+    b = (lin % nhb) / (int)gridDim.y;
+  }
+  const int q0 = blk * BQ;
   const T* qg = static_cast<const T*>(p.q) + b * p.qs[0] + h * p.qs[2];
   const T* kg = static_cast<const T*>(p.k) + b * p.ks[0] + h * p.ks[2];
   const T* vg = static_cast<const T*>(p.v) + b * p.vs[0] + h * p.vs[2];

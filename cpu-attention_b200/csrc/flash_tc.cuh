@@ -155,8 +155,19 @@ __global__ void __launch_bounds__(384, 1) flash_tc_kernel(const __grid_constant_
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nblk = (a.Lq + C::ROWS - 1) / C::ROWS;
-  const int blk = CAUSAL ? nblk - 1 - (int)blockIdx.x : (int)blockIdx.x;  // heavy causal blocks first
-  const int h = blockIdx.y, b = blockIdx.z;
+  // Causal: CTAs are launched in linear block order, so the linear index is
+  // mapped to (query block, head, batch) with the query block slowest and
+  // descending: every (batch, head)'s heaviest block goes first and the grid
+  // ends on the one-tile blocks (longest-processing-time order, which keeps
+  // SMs from idling behind a late heavy block).
+  int blk = (int)blockIdx.x, h = (int)blockIdx.y, b = (int)blockIdx.z;
+  if (CAUSAL) {
+    const int nhb = (int)(gridDim.y * gridDim.z);
+    const int lin = (int)(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z));
+    blk = nblk - 1 - lin / nhb;
+    h = (lin % nhb) % (int)gridDim.y;
+    b = (lin % nhb) / (int)gridDim.y;
+  }
   const int q0 = blk * C::ROWS;
   const int nt0 = tc_tiles(q0, a.Lq, a.Lk, CAUSAL), nt1 = tc_tiles(q0 + C::BM, a.Lq, a.Lk, CAUSAL);
   const int nt = max(nt0, nt1);
