@@ -135,6 +135,17 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
 }
 
+// Pulls the 128-byte line holding `p` into L2 (no register result).
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p) : "memory");
+}
+
+// Pulls `bytes` at `src` into L2 with the bulk-copy engine (no destination;
+// src and bytes 16-byte aligned / multiples).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // L2 policy for data read once (the KV stream): evict first.
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {
   uint64_t pol;

@@ -69,6 +69,7 @@ constexpr int kDecodePageSlots = 24;              // page states in flight to th
 constexpr int kDecodeBlkRing = 512;               // staged block ids per CTA (a ring over the page stream)
 constexpr int kDecodeBlkTask = 256;               // tasks up to this many pages stage their block ids
 constexpr int kSpinSleepNs = 32;                  // sleep between polls of a spinning warp
+constexpr int kDecodeWarmPages = 16;              // pages of its own item each CTA pulls into L2 at the start
 constexpr int kPlanRegs = 4;                      // plan: page counts of 32 sequences per register kept
 
 struct DecodeParams {
@@ -123,6 +124,12 @@ __device__ __forceinline__ int seq_pages(const DecodeParams& p, int i, int* len_
 // Tasks of an item of np pages.
 __device__ __forceinline__ int item_tasks(int np, int U) { return np <= U ? 1 : (np + U - 1) / U; }
 
+// a / b for a >= 0, b > 0, in 32-bit arithmetic whenever a fits (a 64-bit
+// division is a long software sequence on the feeder's critical path).
+__device__ __forceinline__ long long div_pos(long long a, long long b) {
+  return (a <= 0xffffffffLL && b <= 0xffffffffLL) ? (long long)((unsigned)a / (unsigned)b) : a / b;
+}
+
 // Task sizes: items of sequences before icut are cut into tasks of at most
 // Ub pages, the rest (the last sequences, about an eighth of the pages: the
 // tasks handed out last) into tasks of at most Us pages, so that the
@@ -174,8 +181,8 @@ struct TaskWalk {
         const int off = tid - t0;
         t.h = off / t.ntask;
         t.j = off - t.h * t.ntask;
-        t.pg0 = (int)((long long)t.j * t.np / t.ntask);  // even split of the item's pages
-        t.pg1 = (int)((long long)(t.j + 1) * t.np / t.ntask);
+        t.pg0 = (int)div_pos((long long)t.j * t.np, t.ntask);  // even split of the item's pages
+        t.pg1 = (int)div_pos((long long)(t.j + 1) * t.np, t.ntask);
         t.slot = t.ntask > 1 ? s0 + off : -1;
         // keep the scan at this group of 32; the next task is here or later
         tbase = __shfl_sync(0xffffffffu, tincl - tk, 0);
@@ -329,17 +336,17 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
       }
       return np;
     };
-    const long long NP = (long long)warp_sum_i(NP1) * p.H;
+    const int NPh = warp_sum_i(NP1);  // pages per head (every head of a sequence has the same)
+    const long long NP = (long long)NPh * p.H;
     TaskPlan plan;
     plan.Ub = W * p.pages_per_warp;
-    if (NP > (long long)p.task_cap * plan.Ub) plan.Ub = (int)((NP + p.task_cap - 1) / p.task_cap);
+    if (NP > (long long)p.task_cap * plan.Ub) plan.Ub = (int)div_pos(NP + p.task_cap - 1, p.task_cap);
     plan.Us = max(W, plan.Ub / p.tail_div);
     plan.icut = p.B;
     if (plan.Us < plan.Ub) {
       // the first sequence from which on at most an eighth of the pages remain
-      // (in pages per head: every head of a sequence has the same pages)
-      const long long NPh = NP / p.H;
-      const int need = (int)(NPh - NPh / 8);
+      // (in pages per head)
+      const int need = NPh - NPh / 8;
       int base = 0;
       for (int i0 = 0, k = 0; i0 < p.B && plan.icut == p.B; i0 += 32, ++k) {
         const int i = i0 + lane;
@@ -358,7 +365,7 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
       // only when every CTA gets a small task or more, and the split tasks keep
       // within the partial slots (at most 2 np / U slots per split item)
       if (plan.icut == p.B || tail < (long long)gridDim.x * plan.Us ||
-          2 * tail / plan.Us + 2 * NP / plan.Ub > 2LL * p.task_cap)
+          div_pos(2 * tail, plan.Us) + div_pos(2 * NP, plan.Ub) > 2LL * p.task_cap)
         plan.icut = p.B;
     }
     for (int i0 = 0, k = 0; i0 < p.B; i0 += 32, ++k) {
@@ -517,6 +524,39 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
     // does not depend on which warp streamed which page), frees the page
     // slots and the queue entry, then writes the output row, or hands a split
     // task's state to the finisher.
+    // First, while the feeder plans, this warp pulls the query rows and the
+    // page table into L2 (the CTAs share the lines out), so that the loads of
+    // every CTA's first task hit L2 instead of HBM.
+    {
+      const long long qline = ((long long)p.H * E * (long long)sizeof(T) + 127) / 128;  // lines per sequence
+      const long long tline = (p.pt_stride * 4 + 127) / 128;
+      const long long nq = qline * p.B, nl = nq + tline * p.B;
+      for (long long x = blockIdx.x + (long long)gridDim.x * lane; x < nl; x += 32LL * gridDim.x) {
+        const char* a;
+        if (x < nq) {
+          const long long i = div_pos(x, qline);
+          a = reinterpret_cast<const char*>(static_cast<const T*>(p.q) + i * p.q_stride) + (x - i * qline) * 128;
+        } else {
+          const long long y = x - nq, i = div_pos(y, tline);
+          a = reinterpret_cast<const char*>(p.page_table + i * p.pt_stride) + (y - i * tline) * 128;
+        }
+        prefetch_l2(a);
+      }
+      // and the first kDecodeWarmPages pages of item blockIdx.x (sequence
+      // blockIdx.x / H, head blockIdx.x % H): the first tasks' copies wait for
+      // three dependent round trips (lengths, plan and task, block ids), during
+      // which HBM would idle; these pages are read early in the call.
+      if ((long long)blockIdx.x < (long long)p.B * p.H && lane < kDecodeWarmPages && lane < p.pt_stride) {
+        const int i = (int)blockIdx.x / p.H, h = (int)blockIdx.x % p.H;
+        const long long L = min((long long)__ldg(p.lens + i) + p.extra, p.pt_stride * (long long)p.page);
+        const int blk = __ldg(p.page_table + (long long)i * p.pt_stride + lane);
+        if ((long long)lane * p.page < L && blk >= 0 && blk < p.num_blocks) {
+          const long long off = ((long long)blk * p.H + h) * (long long)p.page_bytes;
+          bulk_prefetch_l2(static_cast<const char*>(p.kc) + off, (uint32_t)p.page_bytes);
+          bulk_prefetch_l2(static_cast<const char*>(p.vc) + off, (uint32_t)p.page_bytes);
+        }
+      }
+    }
     T* obase = static_cast<T*>(p.out);
     int nf = 0;  // split tasks handed over
     bool ok = true;
