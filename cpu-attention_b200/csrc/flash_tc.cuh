@@ -30,6 +30,8 @@
 
 #include <cuda.h>
 
+#include <type_traits>
+
 #include "tcgen05.cuh"
 
 namespace ca {
@@ -355,25 +357,36 @@ __global__ void __launch_bounds__(384, 1) flash_tc_kernel(const __grid_constant_
       // P = 2^(scale*s - m) as bf16 pairs, over the first BN/2 S columns
       const uint64_t nm2 = f32x2(-mu, -mu);
       uint64_t sum2 = f32x2(0.f, 0.f);
+      // Two copies of the loop, chosen by one warp-uniform branch: with the
+      // mask test inside a single copy, every element of every tile would pay
+      // for a compare and a select (predicated) although only diagonal tiles
+      // mask. The branch must be uniform (a vote, not the lane's own `full`):
+      // tcgen05.st is .sync.aligned, so all 32 lanes must reach the same one.
+      auto exp_row = [&](auto masked) {
 #pragma unroll
-      for (int ch = 0; ch < C::BN / 32; ++ch) {
-        // packed pair i of this chunk goes to sr[32ch + i]: it was read (as
-        // element 2i >= i of the chunk) before it is overwritten
-        uint32_t* pk = sr + ch * 32;
+        for (int ch = 0; ch < C::BN / 32; ++ch) {
+          // packed pair i of this chunk goes to sr[32ch + i]: it was read (as
+          // element 2i >= i of the chunk) before it is overwritten
+          uint32_t* pk = sr + ch * 32;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int e0 = ch * 32 + 2 * i;
-          const uint64_t xe = fma_f32x2(f32x2(__uint_as_float(sr[e0]), __uint_as_float(sr[e0 + 1])), c2v, nm2);
-          float p0 = exp2_approx(lo_f32(xe)), p1 = exp2_approx(hi_f32(xe));
-          if (!full) {
-            p0 = k0 + e0 <= lim ? p0 : 0.f;
-            p1 = k0 + e0 + 1 <= lim ? p1 : 0.f;
+          for (int i = 0; i < 16; ++i) {
+            const int e0 = ch * 32 + 2 * i;
+            const uint64_t xe = fma_f32x2(f32x2(__uint_as_float(sr[e0]), __uint_as_float(sr[e0 + 1])), c2v, nm2);
+            float p0 = exp2_approx(lo_f32(xe)), p1 = exp2_approx(hi_f32(xe));
+            if constexpr (decltype(masked)::value) {
+              p0 = k0 + e0 <= lim ? p0 : 0.f;
+              p1 = k0 + e0 + 1 <= lim ? p1 : 0.f;
+            }
+            sum2 = add_f32x2(sum2, f32x2(p0, p1));
+            pk[i] = tc::pack_bf16(p0, p1);
           }
-          sum2 = add_f32x2(sum2, f32x2(p0, p1));
-          pk[i] = tc::pack_bf16(p0, p1);
+          tc::tmem_st16(tS + ch * 16, *reinterpret_cast<const uint32_t(*)[16]>(pk));
         }
-        tc::tmem_st16(tS + ch * 16, *reinterpret_cast<const uint32_t(*)[16]>(pk));
-      }
+      };
+      if (__all_sync(0xffffffffu, full))
+        exp_row(std::false_type{});
+      else
+        exp_row(std::true_type{});
       const float sum = lo_f32(sum2) + hi_f32(sum2);
       l = fmaf(l, alpha, sum);
       m = mn;
