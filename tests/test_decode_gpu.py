@@ -325,6 +325,53 @@ def test_engine_route_slots_and_out(dtype):
     assert err <= tol
 
 
+@pytest.mark.parametrize("dtype", cases.DTYPES)
+def test_engine_step_replayed_from_a_cuda_graph(dtype):
+    """The engine's per-layer step (reshape_and_cache, then decode into a
+    preallocated out; examples/ops.py:19-31) captured once in a CUDA graph and
+    replayed with fresh inputs copied into the captured tensors: every replay's
+    output and caches equal those of the same calls made eagerly, bit for bit
+    (neither call synchronises with the host, so the step can be captured)."""
+    from cpu_attention import _kernel as K
+    C = _api()
+    B, H, E, page = 8, 4, 128, 16
+    q, kc, vc, bt, lens = _engine_case(dtype, B=B, H=H, E=E, page=page, maxlen=900, seed=11)
+    btc, lc = bt.cpu(), lens.cpu()
+    slots = torch.tensor([int(btc[i, int(lc[i]) // page]) * page + int(lc[i]) % page for i in range(B)]).to(DEV)
+    after = (lc + 1).to(DEV)
+    kn = torch.empty(B, H, E, dtype=dtype, device=DEV)
+    vn, q3 = torch.empty_like(kn), torch.empty_like(kn)
+    out = torch.empty(B, H, E, dtype=dtype, device=DEV)
+    kc_ref, vc_ref = kc.clone(), vc.clone()
+
+    def step(kcache, vcache, dst):
+        C.reshape_and_cache(kn, vn, kcache, vcache, slots)
+        return K.module().decode(K.runtime(), q3, kcache, vcache, None, None, None, after, bt, None, dst)
+
+    g = torch.Generator().manual_seed(12)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):  # warm-up on the capture stream (its workspace)
+        for t in (kn, vn, q3):
+            t.copy_(torch.randn(B, H, E, generator=g).to(dtype))
+        step(kc.clone(), vc.clone(), torch.empty_like(out))
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        step(kc, vc, out)
+    for _ in range(3):
+        for t in (kn, vn, q3):
+            t.copy_(torch.randn(B, H, E, generator=g).to(dtype))
+        graph.replay()
+        ref = step(kc_ref, vc_ref, None)
+        torch.cuda.synchronize()
+        assert np.array_equal(bits(out), bits(ref))
+        assert np.array_equal(bits(kc), bits(kc_ref)) and np.array_equal(bits(vc), bits(vc_ref))
+    err, tol = north_star_ok(out, cpu_reference(q3, kc, vc, bt, after), dtype)
+    assert err <= tol
+    del graph
+
+
 def test_device_value_errors_are_flagged_not_faulted():
     """Lengths past the page table and table entries past the cache are caught on
     the device (no out-of-bounds access) and raised by raise_status()."""
