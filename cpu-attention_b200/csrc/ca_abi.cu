@@ -97,7 +97,9 @@ bool decode_plan(long long head_dim, long long page, int dtype, const DeviceInfo
   pl->warp_bytes = warp_bytes(stages);
   pl->smem_bytes = warps * pl->warp_bytes + decode_cta_extra(head_dim, warps);
   pl->ctas = dev.sms;
-  pl->pages_per_warp = (o_ppw > 0 && o_ppw <= 64) ? o_ppw : 4;
+  // task unit: 5 pages per streaming warp (measured 1.5% faster than 4 on the
+  // ragged cfg2 workload, equal on the others)
+  pl->pages_per_warp = (o_ppw > 0 && o_ppw <= 64) ? o_ppw : 5;
   pl->task_cap = kTasksPerSm * dev.sms;
   pl->ahead = (o_ah > 0 && o_ah <= 4096) ? o_ah : ca::kDecodeAhead;
   pl->tail_div = (o_td > 0 && o_td <= 16) ? o_td : 2;
