@@ -380,7 +380,7 @@ class ClockSampler:
 # capture of the same command (the files under profiles/ give the commands).
 TRAFFIC = {
     "cfg2": (284.9e6, "profiles/decode_kernel_cfg2.md"),
-    "cfg4": (559.8e6, "profiles/flash_tc_kernel_cfg4.md"),
+    "cfg4": (555.6e6, "profiles/flash_tc_kernel_cfg4.md"),
 }
 
 HOST_HIDE_CYCLES = 400_000  # ~0.2 ms of device spin: longer than the host needs to enqueue one step
