@@ -15,7 +15,8 @@
 //   * Work is cut into tasks: a task is a run of consecutive pages of one
 //     item (sequence i, head h), the item's pages split evenly into
 //     ceil(np / U) tasks, numbered in (sequence, head, piece) order. U is
-//     four pages per streaming warp (more when the workload is huge); the
+//     five pages per streaming warp by default (more when the workload is
+//     huge; the host sets it); the
 //     sequences holding the last eighth of the pages use U / 2, so the tasks
 //     handed out last are short and the SMs run out of work together.
 //   * A persistent grid of one CTA per SM: CTA c starts on task c, then takes
@@ -46,6 +47,11 @@
 //     the fp32 query as broadcast loads; P.V: lanes own 4 dims of a V row.
 //   * Masked keys never reach P.V (the loop stops at the last valid key), so
 //     NaN in unused slots of a page cannot leak (`paged_attn.mojo:686-687`).
+//   * Start-up: the first copies wait for three dependent round trips (the
+//     lengths and the plan, the task's block ids, the pages). Meanwhile the
+//     merger warp, idle until the first task, pulls the query rows, the page
+//     table and the first pages of item blockIdx.x into L2, so HBM is busy
+//     from the first round trip on.
 //   * An append through the page table (one token, or several: a prompt) is
 //     fused: the warp that streams a page holding new tokens patches them
 //     into shared memory after the copy lands and writes them to the cache
