@@ -168,6 +168,23 @@ def test_abi_declines_bad_arguments_without_a_device():
     assert dec(q=None) == K.ENULL
     assert dec(q_stride=100) == K.ELAYOUT
     assert dec(b=0) == K.OK  # nothing to do
+    # the fused prompt append: n tokens per sequence at token stride ts,
+    # sequence stride ss (`flash_attn_interface.py:109-117` in one launch)
+
+    def app(n=3, ts=256, ss=768, kn=p, vn=p, **kw):
+        a = dict(args, **kw)
+        return lib.ca_decode_append(a["q"], a["q_stride"], a["kc"], a["vc"], a["nb"], kn, vn, ss, ts, n,
+                                    a["lens"], a["pt"], a["w"], a["out"], a["b"], a["h"], a["e"], a["page"],
+                                    a["dtype"], a["scale"], a["ws"], a["wsb"], a["stream"])
+
+    assert app(n=0) == K.ESHAPE
+    assert app(kn=None) == K.ESHAPE
+    assert app(vn=None) == K.ESHAPE
+    assert app(ts=100) == K.ELAYOUT  # tokens overlap (token stride < heads * dim)
+    assert app(ss=512) == K.ELAYOUT  # sequences overlap (sequence stride < n * token stride)
+    assert app(n=(1 << 20) + 1, ss=1 << 40) == K.ESHAPE
+    assert app(dtype=7) == K.EDTYPE
+    assert app(b=0) == K.OK
     st = (ctypes.c_int64 * 3)(0, 0, 0)
     assert lib.ca_flash(p, p, p, p, 1, 4, 4, 2, 48, st, st, st, 1.0, 1, 0, None, None) == K.EHEADDIM
     assert lib.ca_flash(p, p, p, p, 1, 0, 4, 2, 64, st, st, st, 1.0, 1, 0, None, None) == K.ESHAPE
