@@ -172,29 +172,36 @@ class Decode:
 
     # end to end through the public API from pinned host buffers
     def e2e_setup(self):
-        pin = lambda t: t.cpu().pin_memory()  # noqa: E731
-        self.h_q = pin(self.q)
-        self.h_kn = pin(self.kn) if self.kn is not None else None
-        self.h_vn = pin(self.vn) if self.vn is not None else None
-        self.h_lens = pin(self.lens)
-        self.h_bt = pin(self.bt)
+        # The step's inputs (query rows, new K/V rows, lengths, page table)
+        # staged in one pinned host buffer and sent with one copy into one
+        # device buffer; the API reads views of it.
+        srcs = [t for t in (self.q, self.kn, self.vn, self.lens, self.bt) if t is not None]
+        offs, total = [], 0
+        for t in srcs:
+            offs.append(total)
+            total += (t.numel() * t.element_size() + 255) // 256 * 256
+        self.h_buf = torch.empty(total, dtype=torch.uint8).pin_memory()
+        self.d_buf = torch.empty(total, dtype=torch.uint8, device=self.q.device)
+
+        def view(buf, t, off):
+            n = t.numel() * t.element_size()
+            return buf[off:off + n].view(t.dtype).view(t.shape)
+
+        views = []
+        for t, off in zip(srcs, offs):
+            view(self.h_buf, t, off).copy_(t.cpu())
+            views.append(view(self.d_buf, t, off))
+        it = iter(views)
+        self.d_q = next(it)
+        self.d_kn = next(it) if self.kn is not None else None
+        self.d_vn = next(it) if self.vn is not None else None
+        self.d_lens, self.d_bt = next(it), next(it)
         self.h_out = torch.empty(self.q.shape, dtype=self.dtype).pin_memory()
-        self.d_q = torch.empty_like(self.q)
-        self.d_kn = torch.empty_like(self.kn) if self.kn is not None else None
-        self.d_vn = torch.empty_like(self.vn) if self.vn is not None else None
-        self.d_lens = torch.empty_like(self.lens)
-        self.d_bt = torch.empty_like(self.bt)
-        h2d = [self.h_q, self.h_kn, self.h_vn, self.h_lens, self.h_bt]
-        self.h2d_bytes = sum(t.numel() * t.element_size() for t in h2d if t is not None)
+        self.h2d_bytes = sum(t.numel() * t.element_size() for t in srcs)
         self.d2h_bytes = self.h_out.numel() * self.h_out.element_size()
 
     def e2e_step(self):
-        self.d_q.copy_(self.h_q, non_blocking=True)
-        if self.d_kn is not None:
-            self.d_kn.copy_(self.h_kn, non_blocking=True)
-            self.d_vn.copy_(self.h_vn, non_blocking=True)
-        self.d_lens.copy_(self.h_lens, non_blocking=True)
-        self.d_bt.copy_(self.h_bt, non_blocking=True)
+        self.d_buf.copy_(self.h_buf, non_blocking=True)
         out = self.C.flash_attn_with_kvcache(self.d_q, self.kc, self.vc, k=self.d_kn, v=self.d_vn,
                                              cache_seqlens=self.d_lens, page_table=self.d_bt)
         self.h_out.copy_(out, non_blocking=True)

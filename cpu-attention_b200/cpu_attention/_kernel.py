@@ -128,8 +128,19 @@ def workspace(device, stream, nbytes=0):
     return ws
 
 
+_WS_BYTES = {}
+
+
 def decode_workspace_bytes(batch, heads, head_dim, page, dtype_code, device_index):
-    return int(library().ca_decode_workspace_bytes(batch, heads, head_dim, page, dtype_code, device_index))
+    """ca_decode_workspace_bytes, remembered per shape (a pure function of its
+    arguments and the device)."""
+    key = (batch, heads, head_dim, page, dtype_code, device_index)
+    n = _WS_BYTES.get(key)
+    if n is None:
+        n = int(library().ca_decode_workspace_bytes(*key))
+        if len(_WS_BYTES) < 4096:
+            _WS_BYTES[key] = n
+    return n
 
 
 def status(device=None, stream=None, reset=True):

@@ -14,19 +14,28 @@ import torch
 from . import _kernel as K
 
 
+_DEVICES = {}
+
+
 def _cuda(*ts):
-    """The common CUDA device of the given tensors, or None."""
-    dev = None
+    """The common CUDA device of the given tensors, or None. (Device indices are
+    compared as ints: building a torch.device per tensor costs more than the
+    rest of the host path.)"""
+    idx = None
     for t in ts:
         if t is None:
             continue
-        if not isinstance(t, torch.Tensor) or t.device.type != "cuda":
+        if not isinstance(t, torch.Tensor) or not t.is_cuda:
             return None
-        if dev is None:
-            dev = t.device
-        elif t.device != dev:
+        d = t.get_device()
+        if idx is None:
+            idx = d
+        elif d != idx:
             return None
-    return dev
+    if idx is None:
+        return None
+    dev = _DEVICES.get(idx)
+    return dev if dev is not None else _DEVICES.setdefault(idx, torch.device("cuda", idx))
 
 
 def _rows_ok(t, hd):
