@@ -81,6 +81,17 @@ def i64x3(values):
     return _I64X3(*values)
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def current_stream(device):
+    """The raw cudaStream_t (as an int) of ``device``'s current stream; torch's
+    raw accessor when it has one (no Stream object is built)."""
+    if _raw_stream is not None:
+        return _raw_stream(device.index)
+    return torch.cuda.current_stream(device).cuda_stream
+
+
 class on_device:
     """Makes ``device`` current for the C calls (kernels launch on the current
     device), at no cost when it already is."""

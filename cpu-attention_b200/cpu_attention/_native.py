@@ -116,7 +116,7 @@ def decode(rt, q, k_cache, v_cache, k, v, slots, lens, page_table, scale, dst):
     if b == 0:
         return out
     lib = K.library()
-    stream = torch.cuda.current_stream(dev).cuda_stream
+    stream = K.current_stream(dev)
     need = K.decode_workspace_bytes(b, heads, hd, page, dt, dev.index)
     if need == 0:
         return None
@@ -160,7 +160,7 @@ def store(rt, key, value, k_cache, v_cache, slots):
         return None
     if n == 0:
         return True
-    stream = torch.cuda.current_stream(dev).cuda_stream
+    stream = K.current_stream(dev)
     ws = K.workspace(dev, stream)
     with K.on_device(dev):
         rc = K.library().ca_store(key.data_ptr(), value.data_ptr(), key.stride(0), k_cache.data_ptr(),
@@ -194,7 +194,7 @@ def flash(rt, q, k, v, scale, causal):
     out = torch.empty((b, sq, heads, hd), dtype=q.dtype, device=dev)
     if b == 0:
         return out
-    stream = torch.cuda.current_stream(dev).cuda_stream
+    stream = K.current_stream(dev)
     arr = (K.i64x3(q.stride()[:3]), K.i64x3(k.stride()[:3]), K.i64x3(v.stride()[:3]))
     ws = K.workspace(dev, stream)
     with K.on_device(dev):
