@@ -60,10 +60,48 @@ def build(force=False, verbose=False):
     return OUT
 
 
+FAST_SRC = os.path.join(CSRC, "fastpath.cpp")
+
+
+def fastpath_out():
+    import sysconfig
+
+    return os.path.join(HERE, "cpu_attention", "_fastpath" + sysconfig.get_config_var("EXT_SUFFIX"))
+
+
+def build_fastpath(force=False, verbose=False):
+    """Compile cpu_attention/_fastpath (the decode host path in C++, a torch
+    extension linked against libca_b200.so) if needed; returns its path."""
+    import sysconfig
+
+    import torch
+    from torch.utils import cpp_extension
+
+    out = fastpath_out()
+    deps = [FAST_SRC, OUT, os.path.join(ROOT, "include", "cpu_attention_b200.h"), os.path.abspath(__file__)]
+    if not force and os.path.exists(out) and all(os.path.getmtime(f) <= os.path.getmtime(out) for f in deps):
+        return out
+    gxx = shutil.which("g++") or "g++"
+    incs = cpp_extension.include_paths(device_type="cuda") + [sysconfig.get_paths()["include"]]
+    libdirs = cpp_extension.library_paths(device_type="cuda")
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    cmd = [gxx, "-O2", "-std=c++17", "-shared", "-fPIC", "-fvisibility=hidden", f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
+           "-DTORCH_EXTENSION_NAME=_fastpath", "-DTORCH_API_INCLUDE_EXTENSION_H",
+           *[f"-I{d}" for d in incs], FAST_SRC, "-o", out + ".tmp",
+           *[f"-L{d}" for d in libdirs], "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_python",
+           f"-L{os.path.dirname(OUT)}", "-lca_b200", "-Wl,-rpath,$ORIGIN", *[f"-Wl,-rpath,{d}" for d in libdirs]]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    subprocess.run(cmd, check=True)
+    os.replace(out + ".tmp", out)
+    return out
+
+
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--verbose", action="store_true")
     a = ap.parse_args()
     print(build(a.force, a.verbose))
+    print(build_fastpath(a.force, a.verbose))
     sys.exit(0)

@@ -125,8 +125,33 @@ _WS_LOCK = threading.Lock()
 _MIN_WS = 1 << 16
 
 
+_FAST = None
+
+
+def fastpath():
+    """The decode host path in C++ (``cpu_attention._fastpath``, built beside
+    the kernel library and linked to it), or None when it is not built or
+    CPU_ATTENTION_SO selects another kernel library."""
+    global _FAST
+    if _FAST is None:
+        _FAST = False
+        if not os.environ.get("CPU_ATTENTION_SO"):
+            library()  # the extension resolves the kernel library already loaded
+            try:
+                from . import _fastpath
+                _FAST = _fastpath
+            except ImportError:
+                _FAST = False
+    return _FAST or None
+
+
 def workspace(device, stream, nbytes=0):
-    """The workspace tensor of (device, stream), at least ``nbytes`` long."""
+    """The workspace tensor of (device, stream), at least ``nbytes`` long (the
+    C++ host path's registry when it is built, so both paths share one)."""
+    fast = fastpath()
+    if fast is not None:
+        index = device.index if device.index is not None else torch.cuda.current_device()
+        return fast.workspace(index, int(stream), nbytes)
     key = (device.index if device.index is not None else torch.cuda.current_device(), int(stream))
     ws = _WS.get(key)
     if ws is None or ws.numel() < nbytes:

@@ -38,6 +38,14 @@ def _cuda(*ts):
     return dev if dev is not None else _DEVICES.setdefault(idx, torch.device("cuda", idx))
 
 
+def _plain_tensors(*ts):
+    return all(type(t) is torch.Tensor for t in ts)
+
+
+def _plain_or_none(*ts):
+    return all(t is None or type(t) is torch.Tensor for t in ts)
+
+
 def _rows_ok(t, hd):
     """Heads and dims contiguous; any token stride (`_C.mojo:68-71`)."""
     return t.stride(-1) == 1 and t.stride(-2) == hd
@@ -74,6 +82,14 @@ def decode(rt, q, k_cache, v_cache, k, v, slots, lens, page_table, scale, dst):
     in the same launch (``ca_decode_append``). Writes ``dst`` when given, else a
     new tensor; returns it, or None (`_C.mojo:87-171`)."""
     del rt
+    fast = K.fastpath()
+    if fast is not None and _plain_tensors(q, k_cache, v_cache, lens, page_table) and _plain_or_none(k, v, slots, dst):
+        # the same checks and call in C++ (cpu_attention/_fastpath)
+        out = fast.decode(q, k_cache, v_cache, k, v, slots, lens, page_table, None if scale is None else float(scale),
+                          dst)
+        if out is not None and K.CHECK:
+            K.raise_status(out.device, K.current_stream(out.device))
+        return out
     dev = _cuda(q, k_cache, v_cache, k, v, slots, lens, page_table, dst)
     if dev is None or not isinstance(q, torch.Tensor):
         return None

@@ -1,0 +1,148 @@
+// The decode entry's host path in C++: the same argument checks as
+// cpu_attention/_native.py::decode (which mirrors `_C.mojo:87-171`), done on
+// at::Tensor fields instead of Python attribute calls, then the C ABI call
+// (ca_decode / ca_decode_append) on the device's current stream. A decode step
+// is short enough (tens of µs) that the Python checks and the ctypes call
+// were the larger part of an end-to-end step's host time.
+//
+// Every decline returns None, exactly where the Python path returns None, so
+// the caller then runs the reference's checks to raise the precise error.
+// The per-(device, stream) workspaces live here too (the Python workspace()
+// hands out the same tensors), so status reads see what the kernels wrote.
+
+#include <torch/extension.h>
+
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+
+#include <algorithm>
+#include <cmath>
+#include <map>
+#include <mutex>
+#include <utility>
+
+#include "../../include/cpu_attention_b200.h"
+
+namespace {
+
+std::mutex g_ws_mutex;
+std::map<std::pair<int, uintptr_t>, at::Tensor> g_ws;
+constexpr int64_t kMinWorkspace = 1 << 16;
+
+// The workspace tensor of (device, stream), at least nbytes long, zero-filled
+// when made (the decode kernel leaves its tickets and counter at zero).
+at::Tensor workspace(int64_t device, uintptr_t stream, int64_t nbytes) {
+  std::lock_guard<std::mutex> lock(g_ws_mutex);
+  const auto key = std::make_pair((int)device, stream);
+  auto it = g_ws.find(key);
+  if (it != g_ws.end() && it->second.numel() >= nbytes) return it->second;
+  const int64_t grown = it == g_ws.end() ? 0 : 2 * it->second.numel();
+  const int64_t size = std::max({nbytes, kMinWorkspace, grown});
+  at::Tensor ws = at::zeros({size}, at::TensorOptions().dtype(at::kByte).device(at::kCUDA, device));
+  g_ws[key] = ws;
+  return ws;
+}
+
+at::Tensor py_workspace(int64_t device, int64_t stream, int64_t nbytes) {
+  return workspace(device, (uintptr_t)stream, nbytes);
+}
+
+// dtype codes of the C ABI (`_kernel.py:17`: float32 0, bfloat16 1)
+int dtype_code(at::ScalarType t) {
+  if (t == at::kFloat) return 0;
+  if (t == at::kBFloat16) return 1;
+  return -1;
+}
+
+bool head_dim_ok(int64_t hd) { return hd == 32 || hd == 64 || hd == 128; }
+
+// heads and dims contiguous; any token stride (`_C.mojo:68-71`)
+bool rows_ok(const at::Tensor& t, int64_t hd) { return t.stride(-1) == 1 && t.stride(-2) == hd; }
+
+bool int_vector(const at::Tensor& t, at::ScalarType dt, int64_t n) {
+  return t.dim() == 1 && t.scalar_type() == dt && t.size(0) == n && t.is_contiguous();
+}
+
+// Returns the output tensor, or None when the call is declined.
+py::object decode(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& vc, const c10::optional<at::Tensor>& k,
+                  const c10::optional<at::Tensor>& v, const c10::optional<at::Tensor>& slots, const at::Tensor& lens,
+                  const at::Tensor& pt, const c10::optional<double>& scale, const c10::optional<at::Tensor>& dst) {
+  // one CUDA device for every tensor
+  if (!q.is_cuda()) return py::none();
+  const auto device = q.device();
+  auto same = [&](const at::Tensor& t) { return t.is_cuda() && t.device() == device; };
+  if (!same(kc) || !same(vc) || !same(lens) || !same(pt)) return py::none();
+  if ((k && !same(*k)) || (v && !same(*v)) || (slots && !same(*slots)) || (dst && !same(*dst))) return py::none();
+
+  const int64_t nd = q.dim();
+  if ((nd != 3 && nd != 4) || (nd == 4 && q.size(1) != 1)) return py::none();
+  const int64_t b = q.size(0), heads = q.size(-2), hd = q.size(-1);
+  const int dt = dtype_code(q.scalar_type());
+  if (dt < 0 || !head_dim_ok(hd) || !rows_ok(q, hd)) return py::none();
+  // caches: [blocks, heads, page, dim], contiguous, matching, page % 16 == 0 (`_C.mojo:74-80`)
+  if (kc.dim() != 4 || vc.sizes() != kc.sizes()) return py::none();
+  if (kc.scalar_type() != q.scalar_type() || vc.scalar_type() != q.scalar_type() || kc.size(1) != heads ||
+      kc.size(3) != hd || kc.size(2) <= 0 || kc.size(2) % 16 || !kc.is_contiguous() || !vc.is_contiguous())
+    return py::none();
+  const int64_t page = kc.size(2);
+  if (pt.dim() != 2 || pt.scalar_type() != at::kInt || pt.size(0) != b || !pt.is_contiguous()) return py::none();
+  if (!int_vector(lens, at::kInt, b)) return py::none();
+  const bool store = k.has_value();
+  int64_t n_new = 1;
+  if (store) {
+    const at::Tensor& kk = *k;
+    const bool multi = nd == 4 && !slots && kk.dim() == 4 && kk.size(0) == b && kk.size(1) > 1 &&
+                       kk.size(2) == heads && kk.size(3) == hd;
+    if (!v || (kk.sizes() != q.sizes() && !multi) || v->sizes() != kk.sizes() || v->strides() != kk.strides())
+      return py::none();
+    if (kk.scalar_type() != q.scalar_type() || v->scalar_type() != q.scalar_type() || !rows_ok(kk, hd))
+      return py::none();
+    if (multi) n_new = kk.size(1);
+  } else if (v) {
+    return py::none();
+  }
+  if (slots && !(store && int_vector(*slots, at::kLong, b))) return py::none();
+  at::Tensor out;
+  if (!dst) {
+    out = at::empty(q.sizes(), q.options());
+  } else {
+    out = *dst;
+    if (out.sizes() != q.sizes() || out.scalar_type() != q.scalar_type() || !out.is_contiguous()) return py::none();
+  }
+  if (b == 0) return py::cast(out);
+
+  const int dev = device.index();
+  const size_t need = ca_decode_workspace_bytes(b, heads, hd, page, dt, dev);
+  if (need == 0) return py::none();
+  const c10::cuda::CUDAGuard guard(device);
+  cudaStream_t stream = c10::cuda::getCurrentCUDAStream(dev).stream();
+  at::Tensor ws = workspace(dev, (uintptr_t)stream, (int64_t)need);
+  const float sc = scale ? (float)*scale : std::nanf("");
+  int rc;
+  if (n_new > 1) {
+    rc = ca_decode_append(q.data_ptr(), q.stride(0), kc.data_ptr(), vc.data_ptr(), kc.size(0), k->data_ptr(),
+                          v->data_ptr(), k->stride(0), k->stride(1), n_new, lens.data_ptr<int32_t>(),
+                          pt.data_ptr<int32_t>(), pt.size(1), out.data_ptr(), b, heads, hd, page, dt, sc,
+                          ws.data_ptr(), (size_t)ws.numel(), stream);
+  } else {
+    rc = ca_decode(q.data_ptr(), q.stride(0), kc.data_ptr(), vc.data_ptr(), kc.size(0),
+                   store ? k->data_ptr() : nullptr, store ? v->data_ptr() : nullptr, store ? k->stride(0) : 0,
+                   slots ? slots->data_ptr<int64_t>() : nullptr, lens.data_ptr<int32_t>(), pt.data_ptr<int32_t>(),
+                   pt.size(1), out.data_ptr(), b, heads, hd, page, dt, sc, ws.data_ptr(), (size_t)ws.numel(),
+                   stream);
+  }
+  if (rc == CA_ECUDA) throw std::runtime_error(std::string("cpu_attention: ") + ca_last_cuda_error());
+  if (rc != CA_OK) return py::none();
+  return py::cast(out);
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "cpu_attention's decode host path in C++ (argument checks and the C ABI call)";
+  m.def("decode", &decode, "paged decode; the output tensor, or None when declined", py::arg("q"), py::arg("k_cache"),
+        py::arg("v_cache"), py::arg("k"), py::arg("v"), py::arg("slots"), py::arg("lens"), py::arg("page_table"),
+        py::arg("scale"), py::arg("dst"));
+  m.def("workspace", &py_workspace, "the workspace tensor of (device, stream), at least nbytes long",
+        py::arg("device"), py::arg("stream"), py::arg("nbytes"));
+}
