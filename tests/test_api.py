@@ -146,6 +146,19 @@ def test_library_exports_every_header_symbol():
     assert lib.ca_build_info().decode().startswith("sm_100a")
 
 
+def test_decode_fast_path_is_built_and_declines_cpu_tensors():
+    """The C++ decode host path is built beside the kernel library, and it
+    declines (None) what the Python path declines -- here, CPU tensors -- so
+    the reference's checks still raise the precise errors."""
+    if os.environ.get("CPU_ATTENTION_SO"):
+        pytest.skip("another kernel library is selected")
+    fast = K.fastpath()
+    assert fast is not None
+    q = torch.zeros(2, 1, 4, 64)
+    lens, pt = torch.zeros(2, dtype=torch.int32), torch.zeros(2, 2, dtype=torch.int32)
+    assert fast.decode(q, q, q, None, None, None, lens, pt, None, None) is None
+
+
 def test_abi_declines_bad_arguments_without_a_device():
     """Argument checks run before any CUDA call."""
     lib = K.library()
