@@ -193,6 +193,13 @@ def flash(rt, q, k, v, scale, causal):
     """flash_attn_func over q/k/v ``[batch, seq, heads, dim]`` (MHA, dims
     contiguous). Returns the output, or None (`_C.mojo:232-316`)."""
     del rt
+    fast = K.fastpath()
+    if fast is not None and _plain_tensors(q, k, v) and (causal is True or causal is False):
+        # the same checks and call in C++ (cpu_attention/_fastpath)
+        out = fast.flash(q, k, v, None if scale is None else float(scale), causal)
+        if out is not None and K.CHECK:
+            K.raise_status(out.device, K.current_stream(out.device))
+        return out
     dev = _cuda(q, k, v)
     if dev is None or q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
         return None

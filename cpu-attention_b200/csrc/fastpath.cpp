@@ -1,9 +1,10 @@
-// The decode entry's host path in C++: the same argument checks as
-// cpu_attention/_native.py::decode (which mirrors `_C.mojo:87-171`), done on
-// at::Tensor fields instead of Python attribute calls, then the C ABI call
-// (ca_decode / ca_decode_append) on the device's current stream. A decode step
-// is short enough (tens of µs) that the Python checks and the ctypes call
-// were the larger part of an end-to-end step's host time.
+// The decode and prefill entries' host path in C++: the same argument checks
+// as cpu_attention/_native.py::decode and ::flash (which mirror
+// `_C.mojo:87-171` and `:232-316`), done on at::Tensor fields instead of
+// Python attribute calls, then the C ABI call (ca_decode / ca_decode_append /
+// ca_flash) on the device's current stream. A decode step is short enough
+// (tens of µs) that the Python checks and the ctypes call were the larger part
+// of an end-to-end step's host time.
 //
 // Every decline returns None, exactly where the Python path returns None, so
 // the caller then runs the reference's checks to raise the precise error.
@@ -136,6 +137,39 @@ py::object decode(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& v
   return py::cast(out);
 }
 
+// flash_attn_func over q/k/v [batch, seq, heads, dim] (MHA, dims contiguous):
+// the checks of cpu_attention/_native.py::flash (`_C.mojo:232-316`), then
+// ca_flash. Returns the output, or None when declined.
+py::object flash(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const c10::optional<double>& scale,
+                 bool causal) {
+  if (!q.is_cuda()) return py::none();
+  const auto device = q.device();
+  if (!k.is_cuda() || k.device() != device || !v.is_cuda() || v.device() != device) return py::none();
+  if (q.dim() != 4 || k.dim() != 4 || v.dim() != 4) return py::none();
+  const int64_t b = q.size(0), sq = q.size(1), heads = q.size(2), hd = q.size(3), sk = k.size(1);
+  const int dt = dtype_code(q.scalar_type());
+  if (dt < 0 || !head_dim_ok(hd) || sq < 1 || sk < 1) return py::none();
+  if (k.size(0) != b || k.size(2) != heads || k.size(3) != hd || k.scalar_type() != q.scalar_type() ||
+      v.scalar_type() != q.scalar_type())
+    return py::none();
+  if (v.sizes() != k.sizes() || q.stride(3) != 1 || k.stride(3) != 1 || v.stride(3) != 1) return py::none();
+  at::Tensor out = at::empty({b, sq, heads, hd}, q.options().memory_format(at::MemoryFormat::Contiguous));
+  if (b == 0) return py::cast(out);
+  const int dev = device.index();
+  const c10::cuda::CUDAGuard guard(device);
+  cudaStream_t stream = c10::cuda::getCurrentCUDAStream(dev).stream();
+  at::Tensor ws = workspace(dev, (uintptr_t)stream, 0);
+  const int64_t qs[3] = {q.stride(0), q.stride(1), q.stride(2)};
+  const int64_t ks[3] = {k.stride(0), k.stride(1), k.stride(2)};
+  const int64_t vs[3] = {v.stride(0), v.stride(1), v.stride(2)};
+  const float sc = scale ? (float)*scale : std::nanf("");
+  const int rc = ca_flash(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), b, sq, sk, heads, hd, qs, ks, vs,
+                          sc, causal ? 1 : 0, dt, static_cast<int32_t*>(ws.data_ptr()), stream);
+  if (rc == CA_ECUDA) throw std::runtime_error(std::string("cpu_attention: ") + ca_last_cuda_error());
+  if (rc != CA_OK) return py::none();
+  return py::cast(out);
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -143,6 +177,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode", &decode, "paged decode; the output tensor, or None when declined", py::arg("q"), py::arg("k_cache"),
         py::arg("v_cache"), py::arg("k"), py::arg("v"), py::arg("slots"), py::arg("lens"), py::arg("page_table"),
         py::arg("scale"), py::arg("dst"));
+  m.def("flash", &flash, "dense prefill; the output tensor, or None when declined", py::arg("q"), py::arg("k"),
+        py::arg("v"), py::arg("scale"), py::arg("causal"));
   m.def("workspace", &py_workspace, "the workspace tensor of (device, stream), at least nbytes long",
         py::arg("device"), py::arg("stream"), py::arg("nbytes"));
 }

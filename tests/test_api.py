@@ -157,6 +157,7 @@ def test_decode_fast_path_is_built_and_declines_cpu_tensors():
     q = torch.zeros(2, 1, 4, 64)
     lens, pt = torch.zeros(2, dtype=torch.int32), torch.zeros(2, 2, dtype=torch.int32)
     assert fast.decode(q, q, q, None, None, None, lens, pt, None, None) is None
+    assert fast.flash(q, q, q, None, True) is None
 
 
 def test_abi_declines_bad_arguments_without_a_device():
