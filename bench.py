@@ -260,15 +260,26 @@ class Prefill:
     kernel_units = units
 
     def e2e_setup(self):
-        self.h = [t.cpu().contiguous().pin_memory() for t in (self.q, self.k, self.v)]
-        self.d = [torch.empty(t.shape, dtype=t.dtype, device=self.dev) for t in self.h]
+        # q, k, v staged in one pinned host buffer and sent with one copy into
+        # one device buffer (contiguous [N, L, H, E] views of it)
+        srcs = (self.q, self.k, self.v)
+        sizes = [t.numel() * t.element_size() for t in srcs]
+        offs = [0]
+        for n in sizes[:-1]:
+            offs.append(offs[-1] + (n + 255) // 256 * 256)
+        total = offs[-1] + (sizes[-1] + 255) // 256 * 256
+        self.h_buf = torch.empty(total, dtype=torch.uint8).pin_memory()
+        self.d_buf = torch.empty(total, dtype=torch.uint8, device=self.dev)
+        self.d = []
+        for t, off, n in zip(srcs, offs, sizes):
+            self.h_buf[off:off + n].view(t.dtype).view(t.shape).copy_(t.cpu())
+            self.d.append(self.d_buf[off:off + n].view(t.dtype).view(t.shape))
         self.h_out = torch.empty(self.q.shape, dtype=self.dtype).pin_memory()
-        self.h2d_bytes = sum(t.numel() * t.element_size() for t in self.h)
+        self.h2d_bytes = sum(sizes)
         self.d2h_bytes = self.h_out.numel() * self.h_out.element_size()
 
     def e2e_step(self):
-        for d, h in zip(self.d, self.h):
-            d.copy_(h, non_blocking=True)
+        self.d_buf.copy_(self.h_buf, non_blocking=True)
         out = self.C.flash_attn_func(*self.d, causal=self.causal)
         self.h_out.copy_(out, non_blocking=True)
 
