@@ -1,39 +1,49 @@
 """Benchmark of the B200 hot path (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload cfg2]
-                    [--impl ours|reference]
+                    [--also cfg4,cfg5] [--impl ours|reference]
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 \
         --master-port P bench.py --gpus N ...
 
-Workloads (the default, cfg2, is the one the metric is
-quoted on; all inputs are seeded synthetic N(0,1) data of the config's shapes):
+Workloads (all inputs are seeded synthetic N(0,1) data
+of the config's shapes; the reference uses no dataset):
 
 * cfg2  paged self-attention decode: flash_attn_with_kvcache, bf16, B=32 H=16
-        E=128 page 16, cache_seqlens uniform in [17, 2047], one appended token.
-        N GPUs: each rank decodes its own 32 sequences (sharded by sequence,
-        weak scaling; no collective on the data path).
+        E=128 page 16, cache_seqlens uniform in [17, 2047], page_table
+        [32, 128] over a seeded permutation of 4096 distinct blocks, one
+        appended token. The headline line. N GPUs: each rank decodes its own
+        32 sequences (sharded by sequence, weak scaling; no collective).
 * cfg3  cross-attention decode (no append), fp32, B=64 H=8 E=64 page 32, 1500
-        tokens per sequence (cfg3e32: head_dim 32).
-* cfg5  engine decode: B=256 H=32 E=128 page 16, lens uniform in [1, 8191];
-        per step reshape_and_cache of 256 tokens (~5% slot -1) then decode with a
-        preallocated out; sequences sharded over ranks in contiguous ranges
-        balanced on context + 16 (strong scaling).
-* cfg1  prefill: flash_attn_func bf16 N=1 L=S=128 H=16 E=64 causal.
+        tokens per sequence in a shuffled block order (cfg3e32: head_dim 32).
+* cfg5  engine decode: B=256 H=32 E=128 page 16, lens uniform in [1, 8191],
+        a shared pool of sum(ceil((len + 1) / 16)) blocks (room for each new
+        token) in a seeded order; per step reshape_and_cache of 256 tokens
+        (~5% slot -1) then decode with a preallocated out; sequences sharded
+        over ranks in contiguous ranges balanced on context + 16 (strong
+        scaling), with and without the output all-gather.
+* cfg1  prefill: flash_attn_func bf16 N=1 L=S=128 H=16 E=64 causal, q/k/v from
+        torch.manual_seed(0).
 * cfg4  prefill: bf16 N=4 L=S=2048 H=32 E=128 causal, q/k/v strided views of a
         fused [N, L, 3, H, E] tensor (cfg4nc: L=512 S=2048 non-causal).
+
+The line is the --workload's record (default cfg2, the config the metric is
+quoted on), plus ``also``: the same record for each --also workload (default
+cfg4 and cfg5, so one run measures decode, prefill and the engine config).
 
 A step is one call of the hot path over the workload's batch, inputs resident
 in HBM; L2 is flushed (a 256 MiB write) before every timed step and the step
 alone is timed with CUDA events on the launching stream; the max over ranks is
-taken. ``e2e`` is the same metric through the public API with the step's inputs
-copied from pinned host memory and the output read back inside the timed
-region. ``roofline`` times the dominant kernel alone. ``cpu_baseline`` times
-the C restatement of the reference's CPU kernel (``oracle/``) on the host cores
-on a bounded sample. ``--impl reference`` times that CPU path as the reference
-arm (rank 0 only).
+taken. ``e2e`` is the same metric through the public API with the step's
+inputs copied from pinned host memory and the output read back inside the
+timed region. ``roofline`` times the dominant kernel alone. ``cpu_baseline``
+times the C restatement of the reference's CPU kernel (``oracle/``) on the
+host's physical cores on a bounded sample, caches flushed (a write sweep of
+twice the LLC) before each call, median. ``--impl reference`` times that CPU
+path as the reference arm, staged on the host alone (rank 0 only).
 """
 
 import argparse
+import datetime
 import json
 import os
 import statistics
@@ -51,6 +61,7 @@ import torch  # noqa: E402
 
 FLUSH_BYTES = 256 << 20
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+CPU_BUDGET_S = 10.0  # wall time of one cpu_baseline (after its warm-up)
 
 
 def peaks():
@@ -63,90 +74,185 @@ def peaks():
         return dict(FALLBACK_PEAKS), "fallback"
 
 
-# ------------------------------------------------------------------ workloads --
-class Decode:
-    """Paged decode workloads (cfg2, cfg3, cfg5)."""
+# ------------------------------------------------------------------ host cores --
+def physical_cores():
+    """Physical cores visible to this process, from the sysfs topology (the
+    reference's thread count, `cpu_attention/_kernel.py:92-104`)."""
+    cores = set()
+    try:
+        for cpu in range(os.cpu_count() or 1):
+            base = f"/sys/devices/system/cpu/cpu{cpu}/topology"
+            with open(f"{base}/core_id") as f, open(f"{base}/physical_package_id") as g:
+                cores.add((g.read().strip(), f.read().strip()))
+    except OSError:
+        cores = set()
+    return len(cores) or (os.cpu_count() or 1)
 
-    def __init__(self, name, rank, world, dev, dtype, B, H, E, page, lens_fn, append, engine=False):
+
+def llc_bytes():
+    """The last-level cache size from sysfs, 32 MiB if unknown
+    (`cpu_attention/_kernel.py:106-117`)."""
+    for idx in (3, 2, 1, 0):
+        try:
+            with open(f"/sys/devices/system/cpu/cpu0/cache/index{idx}/size") as f:
+                text = f.read().strip()
+        except OSError:
+            continue
+        unit = {"K": 1 << 10, "M": 1 << 20}.get(text[-1], 1)
+        return int(text.rstrip("KM")) * unit
+    return 32 << 20
+
+
+class HostFlush:
+    """A write sweep of twice the LLC before each CPU call
+    (`benchmarks/bench.py:112-127`, `:234`)."""
+
+    def __init__(self):
+        torch.set_num_threads(physical_cores())
+        self.buf = torch.zeros(2 * llc_bytes() // 4, dtype=torch.int32)
+
+    def __call__(self):
+        self.buf.add_(1)
+
+
+def time_cpu(fn, flush, warmup, max_calls, budget_s):
+    """Median seconds of fn over up to max_calls calls within budget_s, after
+    `warmup` calls; caches flushed before every call."""
+    for _ in range(warmup):
+        flush()
+        fn()
+    times = []
+    t_start = time.perf_counter()
+    while len(times) < max_calls and (not times or time.perf_counter() - t_start < budget_s):
+        flush()
+        t0 = time.perf_counter()
+        fn()
+        times.append(time.perf_counter() - t0)
+    return statistics.median(times), len(times)
+
+
+# ------------------------------------------------------------------ workloads --
+def _pool(lens, page, extra, g):
+    """Page table over a shared pool of sum(ceil((len + extra) / page)) blocks
+    in a seeded order; padding entries stay 0."""
+    npages = [-(-(int(n) + extra) // page) for n in lens]
+    nblocks = max(1, sum(npages))
+    perm = torch.randperm(nblocks, generator=g).to(torch.int32)
+    bt = torch.zeros(len(lens), max(npages) if npages else 1, dtype=torch.int32)
+    s = 0
+    for i, n in enumerate(npages):
+        bt[i, :n] = perm[s:s + n]
+        s += n
+    return bt, nblocks
+
+
+class DecodeSpec:
+    """The host-side plan of a decode workload: lengths, page table, slots."""
+
+    def __init__(self, name, label, dtype, B, H, E, page, lens_fn, append, engine=False, width=None):
+        self.name, self.label, self.dtype = name, label, dtype
+        self.B_all, self.H, self.E, self.page, self.append, self.engine = B, H, E, page, append, engine
+        self.lens_fn, self.width = lens_fn, width
+
+    def plan(self, rank, world):
+        g = torch.Generator().manual_seed(1234)
+        lens_all = self.lens_fn(g).to(torch.int32)  # the global batch (the same on every rank)
+        if self.engine:  # strong scaling: this rank's contiguous, cost-balanced share
+            ranges = shard_ranges(lens_all, world)
+            lo, hi = ranges[rank]
+            self.counts = [b - a for a, b in ranges]
+            lens = lens_all[lo:hi]
+        else:  # weak scaling: every rank has the full per-GPU batch
+            self.counts = [len(lens_all)] * world
+            lens = lens_all
+        self.global_batch = len(lens_all) * (1 if self.engine else world)
+        self.lens = lens.contiguous()
+        self.B = len(lens)
+        gp = torch.Generator().manual_seed(4321 + rank)
+        if self.width:  # a fixed-width table over distinct blocks (B * width of them)
+            self.nblocks = self.B * self.width
+            self.bt = torch.randperm(self.nblocks, generator=gp).to(torch.int32).view(self.B, self.width).contiguous()
+        else:
+            self.bt, self.nblocks = _pool(self.lens, self.page, 1 if (self.append or self.engine) else 0, gp)
+        extra = 1 if self.append else 0
+        if self.engine:
+            # one new token per sequence at its current length, ~5% padding (-1)
+            ls = [int(n) for n in self.lens]
+            slots = torch.tensor([int(self.bt[i, ls[i] // self.page]) * self.page + ls[i] % self.page
+                                  for i in range(self.B)], dtype=torch.int64)
+            slots[torch.rand(self.B, generator=gp) < 0.05] = -1
+            self.slots = slots
+            self.after = (self.lens + (slots >= 0).to(torch.int32)).contiguous()  # lengths after the store
+            self.attended = [int(n) for n in self.after]
+        else:
+            self.attended = [int(n) + extra for n in self.lens]
+        self.kv_bytes = sum(self.attended) * self.H * self.E * self.dtype.itemsize * 2
+        # token slots of the pre-filled cache (contiguous per sequence)
+        seq = torch.cat([torch.full((int(n),), i, dtype=torch.int64) for i, n in enumerate(self.lens)]) \
+            if self.B else torch.zeros(0, dtype=torch.int64)
+        pos = torch.cat([torch.arange(int(n)) for n in self.lens]) if self.B else torch.zeros(0, dtype=torch.int64)
+        self.fill_slots = self.bt[seq, pos // self.page].long() * self.page + pos % self.page
+        return self
+
+    def config(self, world):
+        lens = [int(n) for n in self.lens]
+        c = {"workload": self.label, "global_batch": self.global_batch, "batch_per_gpu": self.B, "heads": self.H,
+             "head_dim": self.E, "page": self.page, "mean_len": round(sum(lens) / max(1, len(lens)), 1),
+             "append": self.append, "num_blocks": self.nblocks, "table_width": int(self.bt.shape[1]),
+             "parallelism": f"sequence-shard x{world}", "l2": "flushed (256 MiB write) before each step"}
+        if self.engine:
+            c["store_tokens"] = self.B
+            c["store_skipped"] = int((self.slots < 0).sum())
+        return c
+
+
+class Decode:
+    """A decode workload staged on the GPU (the caches written through the
+    product's reshape_and_cache)."""
+
+    kind = "decode"
+
+    def __init__(self, spec, rank, dev):
         import cpu_attention as C
         from cpu_attention import _kernel as K
 
-        self.C, self.K = C, K
-        self.name, self.dev, self.dtype = name, dev, dtype
-        self.H, self.E, self.page, self.append, self.engine = H, E, page, append, engine
-        g = torch.Generator().manual_seed(1234 + rank)
-        lens_all = lens_fn(g)  # the global batch (same on every rank)
-        if engine:  # strong scaling: this rank's contiguous, cost-balanced share
-            lo, hi = shard_ranges(lens_all, world)[rank]
-            lens = lens_all[lo:hi]
-        else:  # weak scaling: every rank has the full per-GPU batch
-            lens = lens_all
-        self.global_batch = len(lens_all) * (1 if engine else world)
-        self.lens_host = lens.to(torch.int32)
-        B = len(lens)
-        self.B = B
-        extra = 1 if append else 0
-        npages = [-(-(int(n) + extra) // page) for n in lens]
-        W = max(npages) if npages else 1
-        nblocks = max(1, sum(npages))
-        perm = torch.randperm(nblocks, generator=g).to(torch.int32)
-        bt = torch.zeros(B, W, dtype=torch.int32)
-        s = 0
-        for i, n in enumerate(npages):
-            bt[i, :n] = perm[s:s + n]
-            s += n
-        self.bt_host = bt
-        self.kc = torch.empty(nblocks, H, page, E, dtype=dtype, device=dev)
+        self.C, self.K, self.s, self.dev = C, K, spec, dev
+        s = spec
+        self.dtype, self.B, self.H, self.E, self.page = s.dtype, s.B, s.H, s.E, s.page
+        self.engine = s.engine
+        self.kc = torch.empty(s.nblocks, s.H, s.page, s.E, dtype=s.dtype, device=dev)
         self.vc = torch.empty_like(self.kc)
-        self.bt = bt.to(dev)
-        self.lens = self.lens_host.to(dev)
+        self.bt = s.bt.to(dev)
+        self.lens = s.lens.to(dev)
         gd = torch.Generator(device=dev).manual_seed(99 + rank)
-        # pre-fill through reshape_and_cache from N(0,1) tokens, in chunks
-        tok_seq = torch.cat([torch.full((int(n),), i, dtype=torch.int64) for i, n in enumerate(lens)]) \
-            if B else torch.zeros(0, dtype=torch.int64)
-        tok_pos = torch.cat([torch.arange(int(n)) for n in lens]) if B else torch.zeros(0, dtype=torch.int64)
-        slots = (bt[tok_seq, tok_pos // page].long() * page + tok_pos % page)
-        for a in range(0, len(slots), 65536):
-            sl = slots[a:a + 65536].to(dev)
-            k = torch.randn(len(sl), H, E, generator=gd, device=dev, dtype=torch.float32).to(dtype)
-            v = torch.randn(len(sl), H, E, generator=gd, device=dev, dtype=torch.float32).to(dtype)
+        for a in range(0, len(s.fill_slots), 65536):
+            sl = s.fill_slots[a:a + 65536].to(dev)
+            k = torch.randn(len(sl), s.H, s.E, generator=gd, device=dev, dtype=torch.float32).to(s.dtype)
+            v = torch.randn(len(sl), s.H, s.E, generator=gd, device=dev, dtype=torch.float32).to(s.dtype)
             C.reshape_and_cache(k, v, self.kc, self.vc, sl)
-        self.q = torch.randn(B, 1, H, E, generator=gd, device=dev, dtype=torch.float32).to(dtype)
-        if append:
-            self.kn = torch.randn(B, 1, H, E, generator=gd, device=dev, dtype=torch.float32).to(dtype)
-            self.vn = torch.randn(B, 1, H, E, generator=gd, device=dev, dtype=torch.float32).to(dtype)
+        rnd = lambda *shape: torch.randn(*shape, generator=gd, device=dev, dtype=torch.float32).to(s.dtype)  # noqa
+        if s.engine:
+            self.q = rnd(s.B, s.H, s.E)
+            self.kn, self.vn = rnd(s.B, s.H, s.E), rnd(s.B, s.H, s.E)
+            self.slots = s.slots.to(dev)
+            self.after = s.after.to(dev)
+            self.out = torch.empty(s.B, s.H, s.E, dtype=s.dtype, device=dev)
         else:
-            self.kn = self.vn = None
-        if engine:
-            # per step: 256 (global) new tokens, ~5% padding slots; this rank's share
-            self.eng_k = torch.randn(B, H, E, generator=gd, device=dev, dtype=torch.float32).to(dtype)
-            self.eng_v = torch.randn(B, H, E, generator=gd, device=dev, dtype=torch.float32).to(dtype)
-            ls = [int(n) for n in lens]
-            es = torch.tensor([int(bt[i, ls[i] // page]) * page + ls[i] % page if ls[i] // page < W else -1
-                               for i in range(B)], dtype=torch.int64)
-            drop = torch.rand(B, generator=g) < 0.05
-            es[drop] = -1
-            self.eng_slots = es.to(dev)
-            # lens after the store: +1 where a token was stored (examples/ops.py:19-25)
-            eng_lens = self.lens_host + (es >= 0).to(torch.int32)
-            self.eng_lens = eng_lens.to(dev)
-            self.out = torch.empty(B, H, E, dtype=dtype, device=dev)
-            attended = [int(n) for n in eng_lens]
-        else:
-            attended = [int(n) + extra for n in lens]
-        self.kv_bytes = sum(attended) * H * E * dtype.itemsize * 2
-        self.attend_lens = torch.tensor(attended, dtype=torch.int32, device=dev)
+            self.q = rnd(s.B, 1, s.H, s.E)
+            self.kn = rnd(s.B, 1, s.H, s.E) if s.append else None
+            self.vn = rnd(s.B, 1, s.H, s.E) if s.append else None
+        self.attend_lens = torch.tensor(s.attended, dtype=torch.int32, device=dev)
         # engine: store + decode; a one-token append is fused into the decode
-        self.launches_per_step = 2 if engine else 1
-        self.counts = [b - a for a, b in shard_ranges(lens_all, world)] if engine else [B] * world
+        self.launches_per_step = 2 if s.engine else 1
+        torch.cuda.synchronize(dev)
 
     # the measured step (device-resident inputs)
     def step(self):
         if self.engine:
-            self.C.reshape_and_cache(self.eng_k, self.eng_v, self.kc, self.vc, self.eng_slots)
+            self.C.reshape_and_cache(self.kn, self.vn, self.kc, self.vc, self.slots)
             K = self.K
-            K.module().decode(K.runtime(), self.q[:, 0], self.kc, self.vc, None, None, None, self.eng_lens, self.bt,
-                              None, self.out)
+            K.module().decode(K.runtime(), self.q, self.kc, self.vc, None, None, None, self.after, self.bt, None,
+                              self.out)
             return self.out
         return self.C.flash_attn_with_kvcache(self.q, self.kc, self.vc, k=self.kn, v=self.vn, cache_seqlens=self.lens,
                                               page_table=self.bt)
@@ -156,32 +262,34 @@ class Decode:
     def gather_step(self):
         from cpu_attention.shard import gather_outputs
         out = self.step()
-        return gather_outputs(out.reshape(out.shape[0], -1), self.counts)
+        return gather_outputs(out.reshape(out.shape[0], -1), self.s.counts)
 
     # the dominant kernel alone: decode over the attended lengths, no store
     def kernel_step(self):
         K = self.K
-        K.module().decode(K.runtime(), self.q, self.kc, self.vc, None, None, None, self.attend_lens, self.bt,
-                          None, None)
+        q = self.q if self.q.dim() == 3 else self.q[:, 0]
+        K.module().decode(K.runtime(), q, self.kc, self.vc, None, None, None, self.attend_lens, self.bt, None, None)
 
     def units(self):
-        return self.kv_bytes
+        return self.s.kv_bytes
 
-    def kernel_units(self):
-        return self.kv_bytes
+    kernel_units = units
 
-    # end to end through the public API from pinned host buffers
+    # end to end through the public API from pinned host buffers: the step's
+    # inputs (query rows, new K/V rows, slots, lengths, page table) staged in
+    # one pinned host buffer and sent with one copy into one device buffer,
+    # as an engine stages them; the API reads views of it
     def e2e_setup(self):
-        # The step's inputs (query rows, new K/V rows, lengths, page table)
-        # staged in one pinned host buffer and sent with one copy into one
-        # device buffer; the API reads views of it.
-        srcs = [t for t in (self.q, self.kn, self.vn, self.lens, self.bt) if t is not None]
+        if self.engine:
+            srcs = [self.q, self.kn, self.vn, self.slots, self.after, self.bt]
+        else:
+            srcs = [t for t in (self.q, self.kn, self.vn, self.lens, self.bt) if t is not None]
         offs, total = [], 0
         for t in srcs:
             offs.append(total)
             total += (t.numel() * t.element_size() + 255) // 256 * 256
         self.h_buf = torch.empty(total, dtype=torch.uint8).pin_memory()
-        self.d_buf = torch.empty(total, dtype=torch.uint8, device=self.q.device)
+        self.d_buf = torch.empty(total, dtype=torch.uint8, device=self.dev)
 
         def view(buf, t, off):
             n = t.numel() * t.element_size()
@@ -191,66 +299,123 @@ class Decode:
         for t, off in zip(srcs, offs):
             view(self.h_buf, t, off).copy_(t.cpu())
             views.append(view(self.d_buf, t, off))
-        it = iter(views)
-        self.d_q = next(it)
-        self.d_kn = next(it) if self.kn is not None else None
-        self.d_vn = next(it) if self.vn is not None else None
-        self.d_lens, self.d_bt = next(it), next(it)
+        self.d = views
         self.h_out = torch.empty(self.q.shape, dtype=self.dtype).pin_memory()
         self.h2d_bytes = sum(t.numel() * t.element_size() for t in srcs)
         self.d2h_bytes = self.h_out.numel() * self.h_out.element_size()
 
     def e2e_step(self):
         self.d_buf.copy_(self.h_buf, non_blocking=True)
-        out = self.C.flash_attn_with_kvcache(self.d_q, self.kc, self.vc, k=self.d_kn, v=self.d_vn,
-                                             cache_seqlens=self.d_lens, page_table=self.d_bt)
+        if self.engine:
+            q, kn, vn, slots, after, bt = self.d
+            self.C.reshape_and_cache(kn, vn, self.kc, self.vc, slots)
+            K = self.K
+            out = K.module().decode(K.runtime(), q, self.kc, self.vc, None, None, None, after, bt, None, self.out)
+        else:
+            it = iter(self.d)
+            q = next(it)
+            kn = next(it) if self.kn is not None else None
+            vn = next(it) if self.vn is not None else None
+            lens, bt = next(it), next(it)
+            out = self.C.flash_attn_with_kvcache(q, self.kc, self.vc, k=kn, v=vn, cache_seqlens=lens, page_table=bt)
         self.h_out.copy_(out, non_blocking=True)
 
-    # the C restatement of the reference kernel on the host cores
-    def cpu_setup(self):
-        self.c_kc, self.c_vc = self.kc.cpu(), self.vc.cpu()
-        self.c_q = self.q.cpu().reshape(self.B, self.H, self.E).contiguous()
-        self.c_kn = self.kn.cpu().reshape(self.c_q.shape).contiguous() if self.kn is not None else None
-        self.c_vn = self.vn.cpu().reshape(self.c_q.shape).contiguous() if self.vn is not None else None
+    # the C restatement of the reference kernel on the host cores, on the
+    # first `max_seqs` sequences (their pages gathered into a compact cache)
+    def cpu_setup(self, max_seqs=64):
+        s = self.s
+        n = min(self.B, max_seqs)
+        npg = [-(-a // s.page) for a in s.attended[:n]]
+        W = max(npg)
+        blocks = torch.cat([s.bt[i, :npg[i]].long() for i in range(n)])
+        if self.engine:  # the store goes to the sequence's page at its length
+            blocks = torch.unique(torch.cat([blocks, s.bt[:n].long().flatten()]))
+        else:
+            blocks = torch.unique(blocks)
+        remap = torch.full((s.nblocks,), 0, dtype=torch.int32)
+        remap[blocks] = torch.arange(len(blocks), dtype=torch.int32)
+        self.c_bt = remap[s.bt[:n, :W].long()].contiguous()
+        idx = blocks.to(self.dev)
+        self.c_kc, self.c_vc = self.kc[idx].cpu(), self.vc[idx].cpu()
+        q = self.q if self.q.dim() == 3 else self.q[:, 0]
+        self.c_q = q[:n].cpu().contiguous()
+        self.c_kn = self.kn.reshape(self.B, self.H, self.E)[:n].cpu().contiguous() if self.kn is not None else None
+        self.c_vn = self.vn.reshape(self.B, self.H, self.E)[:n].cpu().contiguous() if self.vn is not None else None
         self.c_out = torch.empty(self.c_q.shape, dtype=self.dtype)
+        if self.engine:
+            sl = s.slots[:n]
+            blk = torch.where(sl >= 0, remap[(sl.clamp(min=0) // s.page)].long(), torch.full_like(sl, -1))
+            self.c_slots = torch.where(sl >= 0, blk * s.page + sl % s.page, sl).contiguous()
+            self.c_lens = s.after[:n].contiguous()
+        else:
+            self.c_slots, self.c_lens = None, s.lens[:n].contiguous()
+        self.cpu_units = sum(s.attended[:n]) * self.H * self.E * self.dtype.itemsize * 2
+        self.cpu_sample = f"the first {n} of {self.B} sequences" if n < self.B else "the full workload"
 
     def cpu_step(self, threads):
         from oracle import cpu as ORACLE
-        ORACLE.decode(self.c_q, self.c_kc, self.c_vc, self.lens_host, self.bt_host, self.c_out, k_new=self.c_kn,
-                      v_new=self.c_vn, threads=threads)
+        ORACLE.decode(self.c_q, self.c_kc, self.c_vc, self.c_lens, self.c_bt, self.c_out, k_new=self.c_kn,
+                      v_new=self.c_vn, slots=self.c_slots, threads=threads)
 
     def config(self, world):
-        lens = [int(n) for n in self.lens_host]
-        return {"workload": self.name, "global_batch": self.global_batch, "batch_per_gpu": self.B,
-                "heads": self.H, "head_dim": self.E, "page": self.page,
-                "mean_len": round(sum(lens) / max(1, len(lens)), 1), "append": self.append,
-                "parallelism": f"sequence-shard x{world}", "l2": "flushed (256 MiB write) before each step"}
+        return self.s.config(world)
+
+
+class HostDecode(Decode):
+    """The reference arm's decode workload, staged on the host alone: caches
+    written by the oracle's restatement of the store (no device, none of the
+    product's libraries), N(0,1) data from a CPU generator."""
+
+    def __init__(self, spec):
+        from oracle import cpu as ORACLE
+        s = spec
+        self.s, self.dtype, self.B, self.H, self.E, self.page, self.engine = s, s.dtype, s.B, s.H, s.E, s.page, \
+            s.engine
+        g = torch.Generator().manual_seed(99)
+        self.c_kc = torch.empty(s.nblocks, s.H, s.page, s.E, dtype=s.dtype)
+        self.c_vc = torch.empty_like(self.c_kc)
+        for a in range(0, len(s.fill_slots), 65536):
+            sl = s.fill_slots[a:a + 65536].contiguous()
+            k = torch.randn(len(sl), s.H, s.E, generator=g).to(s.dtype)
+            v = torch.randn(len(sl), s.H, s.E, generator=g).to(s.dtype)
+            ORACLE.store(k, v, self.c_kc, self.c_vc, sl)
+        self.c_q = torch.randn(s.B, s.H, s.E, generator=g).to(s.dtype)
+        new = s.append or s.engine
+        self.c_kn = torch.randn(s.B, s.H, s.E, generator=g).to(s.dtype) if new else None
+        self.c_vn = torch.randn(s.B, s.H, s.E, generator=g).to(s.dtype) if new else None
+        self.c_bt = s.bt
+        self.c_slots = s.slots if s.engine else None
+        self.c_lens = s.after if s.engine else s.lens
+        self.c_out = torch.empty(s.B, s.H, s.E, dtype=s.dtype)
+        self.cpu_units = s.kv_bytes
+        self.cpu_sample = "the full workload per step"
 
 
 class Prefill:
     """Dense prefill workloads (cfg1, cfg4, cfg4nc)."""
 
-    def __init__(self, name, rank, world, dev, N, L, S, H, E, causal, fused):
-        import cpu_attention as C
+    kind = "prefill"
 
-        self.C, self.name, self.dev = C, name, dev
-        self.N, self.L, self.S, self.H, self.E, self.causal = N, L, S, H, E, causal
+    def __init__(self, name, label, rank, world, dev, N, L, S, H, E, causal, fused):
+        self.name, self.label, self.dev = name, label, dev
+        self.N, self.L, self.S, self.H, self.E, self.causal, self.fused = N, L, S, H, E, causal, fused
         self.dtype = torch.bfloat16
-        gd = torch.Generator(device=dev).manual_seed(7 + rank)
         if fused:
-            qkv = torch.randn(N, S, 3, H, E, generator=gd, device=dev, dtype=torch.float32).to(self.dtype)
-            self.q, self.k, self.v = qkv[:, S - L:, 0], qkv[:, :, 1], qkv[:, :, 2]
+            gd = torch.Generator(device=dev).manual_seed(7 + rank) if dev is not None else None
+            self.qkv = torch.randn(N, S, 3, H, E, generator=gd, device=dev, dtype=torch.float32).to(self.dtype)
+            self.q, self.k, self.v = self.qkv[:, S - L:, 0], self.qkv[:, :, 1], self.qkv[:, :, 2]
         else:
-            self.q = torch.randn(N, L, H, E, generator=gd, device=dev, dtype=torch.float32).to(self.dtype)
-            self.k = torch.randn(N, S, H, E, generator=gd, device=dev, dtype=torch.float32).to(self.dtype)
-            self.v = torch.randn(N, S, H, E, generator=gd, device=dev, dtype=torch.float32).to(self.dtype)
+            torch.manual_seed(0)
+            q, k, v = (torch.randn(N, n, H, E, dtype=self.dtype) for n in (L, S, S))
+            self.q, self.k, self.v = (x.to(dev) if dev is not None else x for x in (q, k, v))
         pairs = sum(min(S, max(0, i + S - L + 1)) for i in range(L)) if causal else L * S
         self.flops = 4 * N * H * E * pairs
         self.global_batch = N * world
         self.launches_per_step = 1
 
     def step(self):
-        self.C.flash_attn_func(self.q, self.k, self.v, causal=self.causal)
+        import cpu_attention as C
+        return C.flash_attn_func(self.q, self.k, self.v, causal=self.causal)
 
     kernel_step = step
 
@@ -260,9 +425,10 @@ class Prefill:
     kernel_units = units
 
     def e2e_setup(self):
-        # q, k, v staged in one pinned host buffer and sent with one copy into
-        # one device buffer (contiguous [N, L, H, E] views of it)
-        srcs = (self.q, self.k, self.v)
+        # the step's inputs in one pinned host buffer, sent with one copy: the
+        # fused [N, S, 3, H, E] tensor whose strided views q/k/v are (cfg4), or
+        # q, k, v back to back (cfg1)
+        srcs = (self.qkv,) if self.fused else (self.q, self.k, self.v)
         sizes = [t.numel() * t.element_size() for t in srcs]
         offs = [0]
         for n in sizes[:-1]:
@@ -270,32 +436,43 @@ class Prefill:
         total = offs[-1] + (sizes[-1] + 255) // 256 * 256
         self.h_buf = torch.empty(total, dtype=torch.uint8).pin_memory()
         self.d_buf = torch.empty(total, dtype=torch.uint8, device=self.dev)
-        self.d = []
+        dev_views = []
         for t, off, n in zip(srcs, offs, sizes):
             self.h_buf[off:off + n].view(t.dtype).view(t.shape).copy_(t.cpu())
-            self.d.append(self.d_buf[off:off + n].view(t.dtype).view(t.shape))
+            dev_views.append(self.d_buf[off:off + n].view(t.dtype).view(t.shape))
+        if self.fused:
+            qkv = dev_views[0]
+            self.d = (qkv[:, self.S - self.L:, 0], qkv[:, :, 1], qkv[:, :, 2])
+        else:
+            self.d = tuple(dev_views)
         self.h_out = torch.empty(self.q.shape, dtype=self.dtype).pin_memory()
         self.h2d_bytes = sum(sizes)
         self.d2h_bytes = self.h_out.numel() * self.h_out.element_size()
 
     def e2e_step(self):
+        import cpu_attention as C
         self.d_buf.copy_(self.h_buf, non_blocking=True)
-        out = self.C.flash_attn_func(*self.d, causal=self.causal)
+        out = C.flash_attn_func(*self.d, causal=self.causal)
         self.h_out.copy_(out, non_blocking=True)
 
-    def cpu_setup(self):
-        # a bounded sample: the first head of the first batch entry
-        self.c = [t[:1, :, :1].cpu() for t in (self.q, self.k, self.v)]
+    def cpu_setup(self, max_seqs=None):
+        # a bounded sample: the first heads of the first batch entry, one per
+        # physical core
+        nh = min(self.H, physical_cores())
+        self.c = [t[:1, :, :nh].cpu() for t in (self.q, self.k, self.v)]
         self.c_out = torch.empty(self.c[0].shape, dtype=self.dtype)
-        self.cpu_units = self.flops / (self.N * self.H)
+        self.cpu_units = self.flops * nh / (self.N * self.H)
+        self.cpu_sample = f"{nh} (batch, head) pairs of the workload"
 
     def cpu_step(self, threads):
         from oracle import cpu as ORACLE
         ORACLE.flash(*self.c, self.c_out, causal=self.causal, threads=threads)
 
     def config(self, world):
-        return {"workload": self.name, "global_batch": self.global_batch, "seq_q": self.L, "seq_k": self.S,
+        return {"workload": self.label, "global_batch": self.global_batch, "seq_q": self.L, "seq_k": self.S,
                 "heads": self.H, "head_dim": self.E, "causal": self.causal,
+                "inputs": ("strided views of a fused [N, S, 3, H, E] tensor" if self.fused
+                           else "contiguous, torch.manual_seed(0)"),
                 "parallelism": f"batch-shard x{world}", "l2": "flushed (256 MiB write) before each step"}
 
 
@@ -306,37 +483,43 @@ def shard_ranges(lens, world):
     return balanced_ranges([int(n) for n in lens], world)
 
 
+DECODE = {
+    "cfg2": lambda: DecodeSpec("cfg2", "cfg2: flash_attn_with_kvcache bf16 B=32 H=16 E=128 page16 lens~U[17,2047] "
+                               "+1 append", torch.bfloat16, 32, 16, 128, 16,
+                               lambda g: torch.randint(17, 2048, (32,), generator=g), append=True, width=128),
+    "cfg3": lambda: DecodeSpec("cfg3", "cfg3: cross-attention decode fp32 B=64 H=8 E=64 page32 len=1500 no append",
+                               torch.float32, 64, 8, 64, 32, lambda g: torch.full((64,), 1500), append=False),
+    "cfg3e32": lambda: DecodeSpec("cfg3e32", "cfg3e32: cross-attention decode fp32 B=64 H=8 E=32 page32 len=1500 "
+                                  "no append", torch.float32, 64, 8, 32, 32, lambda g: torch.full((64,), 1500),
+                                  append=False),
+    "cfg5": lambda: DecodeSpec("cfg5", "cfg5: engine decode bf16 B=256 H=32 E=128 page16 lens~U[1,8191] "
+                               "store+decode out=", torch.bfloat16, 256, 32, 128, 16,
+                               lambda g: torch.randint(1, 8192, (256,), generator=g), append=False, engine=True),
+}
+PREFILL = {
+    "cfg1": ("cfg1: flash_attn_func bf16 N=1 L=S=128 H=16 E=64 causal", 1, 128, 128, 16, 64, True, False),
+    "cfg4": ("cfg4: flash_attn_func bf16 N=4 L=S=2048 H=32 E=128 causal fused-QKV views", 4, 2048, 2048, 32, 128,
+             True, True),
+    "cfg4nc": ("cfg4nc: flash_attn_func bf16 N=4 L=512 S=2048 H=32 E=128 non-causal fused-QKV views", 4, 512, 2048,
+               32, 128, False, True),
+}
+
+
 def make_workload(name, rank, world, dev):
-    if name == "cfg2":
-        return Decode("cfg2: flash_attn_with_kvcache bf16 B=32 H=16 E=128 page16 lens~U[17,2047] +1 append",
-                      rank, world, dev, torch.bfloat16, 32, 16, 128, 16,
-                      lambda g: torch.randint(17, 2048, (32,), generator=g), append=True)
-    if name in ("cfg3", "cfg3e32"):
-        E = 64 if name == "cfg3" else 32
-        return Decode(f"{name}: cross-attention decode fp32 B=64 H=8 E={E} page32 len=1500 no append",
-                      rank, world, dev, torch.float32, 64, 8, E, 32,
-                      lambda g: torch.full((64,), 1500, dtype=torch.int64), append=False)
-    if name == "cfg5":
-        return Decode("cfg5: engine decode bf16 B=256 H=32 E=128 page16 lens~U[1,8191] store+decode out=",
-                      rank, world, dev, torch.bfloat16, 256, 32, 128, 16,
-                      lambda g: torch.randint(1, 8192, (256,), generator=g), append=False, engine=True)
-    if name == "cfg1":
-        return Prefill("cfg1: flash_attn_func bf16 N=1 L=S=128 H=16 E=64 causal", rank, world, dev,
-                       1, 128, 128, 16, 64, True, False)
-    if name == "cfg4":
-        return Prefill("cfg4: flash_attn_func bf16 N=4 L=S=2048 H=32 E=128 causal fused-QKV views", rank, world,
-                       dev, 4, 2048, 2048, 32, 128, True, True)
-    if name == "cfg4nc":
-        return Prefill("cfg4nc: flash_attn_func bf16 N=4 L=512 S=2048 H=32 E=128 non-causal fused-QKV views",
-                       rank, world, dev, 4, 512, 2048, 32, 128, False, True)
+    if name in DECODE:
+        return Decode(DECODE[name]().plan(rank, world), rank, dev)
+    if name in PREFILL:
+        label, *shape = PREFILL[name]
+        return Prefill(name, label, rank, world, dev, *shape)
     raise SystemExit(f"unknown workload {name}")
 
 
 # --------------------------------------------------------------------- timing --
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """nvidia-smi clocks and throttle reasons sampled every 50 ms; each
+    workload reads the samples of its own time window."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
 
@@ -346,8 +529,7 @@ class ClockSampler:
         self.gpus = gpus
 
     def start(self):
-        """Start sampling every 50 ms; returns once the first sample is in
-        (at most ~5 s), so the timed region that follows is covered."""
+        """Start sampling; returns once the first sample is in (at most ~5 s)."""
         try:
             fd, self.path = tempfile.mkstemp(suffix=".csv")
             os.close(fd)
@@ -364,38 +546,48 @@ class ClockSampler:
                 break
             time.sleep(0.02)
 
-    def stop(self):
+    def window(self, t0, t1):
+        """Clocks of the samples taken in [t0, t1] (wall time, seconds)."""
         if self.proc is None:
             return None
+        self.fh.flush()
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        a, b = datetime.datetime.fromtimestamp(t0), datetime.datetime.fromtimestamp(t1)
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f")
+                    if ts < a or ts > b:
+                        continue
+                    sm.append(float(parts[2]))
+                    mx = max(mx, float(parts[3]))
+                except ValueError:
+                    continue
+                for n, v in zip(names, parts[5:9]):
+                    if v.lower().startswith("active"):
+                        reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+    def stop(self):
+        if self.proc is None:
+            return
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
         self.fh.close()
-        sm, mx, reasons = [], 0.0, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        with open(self.path) as f:
-            for line in f:
-                parts = [p.strip() for p in line.split(",")]
-                if len(parts) < 8:
-                    continue
-                try:
-                    sm.append(float(parts[1]))
-                    mx = max(mx, float(parts[2]))
-                except ValueError:
-                    continue
-                for n, v in zip(names, parts[4:8]):
-                    if v.lower().startswith("active"):
-                        reasons.add(n)
         os.unlink(self.path)
-        if not sm:
-            return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
 # DRAM bytes (read + write) of one launch of the roofline kernel, from one ncu
-# capture of the same command (the files under profiles/ give the commands).
+# capture of the same workload (the files under profiles/ give the commands).
 TRAFFIC = {
     "cfg2": (284.9e6, "profiles/decode_kernel_cfg2.md"),
     "cfg4": (555.6e6, "profiles/flash_tc_kernel_cfg4.md"),
@@ -458,57 +650,116 @@ def barrier(world):
 
 
 def metric_of(wl):
-    if isinstance(wl, Prefill):
+    if wl.kind == "prefill":
         return "prefill bf16 TFLOP/s", "TFLOP/s", 1e12
     return "paged-decode KV GB/s", "GB/s", 1e9
 
 
-def cpu_baseline(wl, threads, budget_s=20.0):
-    """The oracle's C restatement of the reference kernel on the host cores,
-    3 warm-up + up to 10 timed calls within about budget_s seconds; median."""
+def cpu_baseline(wl, flush, threads):
+    """The oracle's C restatement of the reference kernel on the host's
+    physical cores: 3 warm-up + up to 10 timed calls within ~CPU_BUDGET_S,
+    caches flushed before each, median."""
     wl.cpu_setup()
-    for _ in range(2):
-        wl.cpu_step(threads)
-    times = []
-    t_start = time.perf_counter()
-    while len(times) < 10 and (time.perf_counter() - t_start) < budget_s:
-        t0 = time.perf_counter()
-        wl.cpu_step(threads)
-        times.append(time.perf_counter() - t0)
-    sec = statistics.median(times)
-    units = getattr(wl, "cpu_units", wl.units())
-    return sec, units, len(times)
+    sec, n = time_cpu(lambda: wl.cpu_step(threads), flush, 3, 10, CPU_BUDGET_S)
+    return sec, wl.cpu_units, n
+
+
+def measure(wl, name, args, world, rank, sampler, flush_host):
+    """One workload's record: the device-timed step, the roofline kernel, e2e,
+    the N > 1 gather (decode), and at N = 1 the CPU baseline."""
+    dev, stream = wl.dev, torch.cuda.current_stream(wl.dev)
+    flush_buf = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    flush = lambda: flush_buf.fill_(1)  # noqa: E731
+    metric, unit, scale = metric_of(wl)
+    barrier(world)
+    t_begin = time.time()
+    step_ms = timed(wl.step, args.steps, args.warmup, flush, stream)
+    barrier(world)
+    total_ms = max_over_ranks(sum(step_ms), world)
+    units = sum_over_ranks(wl.units(), world)
+    ms_per_step = total_ms / args.steps
+    value = units / (ms_per_step * 1e-3) / scale
+
+    # the dominant kernel alone (roofline)
+    kern_ms = timed(wl.kernel_step, args.steps, 2, flush, stream)
+    kern_avg = statistics.mean(kern_ms)
+    pk, pk_kind = peaks()
+    if wl.kind == "prefill":
+        achieved = wl.kernel_units() / (kern_avg * 1e-3) / 1e12
+        peak, bound, runit = pk["bf16_tflops"], "tensor", "TFLOP/s"
+    else:
+        achieved = wl.kernel_units() / (kern_avg * 1e-3) / 1e9
+        peak, bound, runit = pk["hbm_gbs"], "hbm", "GB/s"
+    achieved = -max_over_ranks(-achieved, world)  # the slowest rank
+    roofline = {"bound": bound, "achieved": round(achieved, 2), "peak": peak, "peak_kind": pk_kind, "unit": runit,
+                "frac": round(achieved / peak, 4),
+                "traffic": TRAFFIC[name][0] if name in TRAFFIC else None,
+                "traffic_source": TRAFFIC[name][1] if name in TRAFFIC else None,
+                "kernel_ms": round(kern_avg, 4)}
+
+    # end to end through the public API, host buffers
+    wl.e2e_setup()
+    e2e_ms = timed(wl.e2e_step, args.steps, 2, flush, stream, hide_host=False)
+    e2e_total = max_over_ranks(sum(e2e_ms), world)
+    e2e_value = units / (e2e_total / args.steps * 1e-3) / scale
+
+    # N > 1 decode: the same step with the output all-gather after it
+    with_gather = None
+    if world > 1 and wl.kind == "decode":
+        g_ms = timed(wl.gather_step, args.steps, 2, flush, stream)
+        g_total = max_over_ranks(sum(g_ms), world)
+        with_gather = {"value": round(units / (g_total / args.steps * 1e-3) / scale, 3), "unit": unit,
+                       "ms_per_step": round(g_total / args.steps, 4), "collective": "all_gather_into_tensor"}
+    barrier(world)
+    t_end = time.time()
+    rec = {"metric": metric, "value": round(value, 3), "unit": unit, "n_gpus": world, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "us_per_call": round(ms_per_step * 1e3, 2),
+           "higher_is_better": True, "scaling": "strong" if getattr(wl, "engine", False) else "weak",
+           "vs_baseline": None, "dtype": str(wl.dtype).split(".")[-1], "data": "synthetic",
+           "config": wl.config(world), "roofline": roofline,
+           "e2e": {"value": round(e2e_value, 3), "unit": unit, "h2d_bytes_per_step": wl.h2d_bytes,
+                   "d2h_bytes_per_step": wl.d2h_bytes, "ms_per_step": round(e2e_total / args.steps, 4)},
+           "gpu_launches": wl.launches_per_step * args.steps,
+           "clocks": sampler.window(t_begin, t_end) if sampler else None}
+    if with_gather is not None:
+        rec["with_gather"] = with_gather
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = physical_cores()
+        sec, cunits, n = cpu_baseline(wl, flush_host, threads)
+        rec["cpu_baseline"] = {"value": round(cunits / sec / scale, 4), "unit": unit, "cores": threads,
+                               "kind": "port", "sample": f"{wl.cpu_sample}, median of {n} calls, caches flushed",
+                               "ms_per_call": round(sec * 1e3, 3)}
+    return rec
 
 
 def run_reference(args):
     """The reference arm: the C restatement of the reference's CPU kernel
-    (`oracle/`), the reference's own Mojo kernel being unbuildable here, timed
-    on all host threads, rank 0 only."""
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
+    (`oracle/`; the reference's own Mojo kernel cannot be built here), staged
+    and timed on the host alone -- none of this repository's CUDA libraries is
+    loaded -- on its physical cores, caches flushed before every call, the
+    median of --steps calls after --warmup. Rank 0 only."""
+    if int(os.environ.get("RANK", "0")) != 0:
         return 0
-    threads = os.cpu_count() or 1
-    dev = torch.device("cuda", 0) if torch.cuda.is_available() else None
-    wl = make_workload(args.workload, 0, 1, dev)
+    if args.workload not in DECODE:
+        label, *shape = PREFILL[args.workload]
+        wl = Prefill(args.workload, label, 0, 1, None, *shape)
+        wl.cpu_setup()
+    else:
+        spec = DECODE[args.workload]()
+        if spec.engine:
+            raise SystemExit("the reference arm stages cfg2/cfg3 decode and the prefill configs")
+        wl = HostDecode(spec.plan(0, 1))
+    threads = physical_cores()
+    flush = HostFlush()
     metric, unit, scale = metric_of(wl)
-    wl.cpu_setup()
-    for _ in range(args.warmup):
-        wl.cpu_step(threads)
-    times = []
-    for _ in range(args.steps):
-        t0 = time.perf_counter()
-        wl.cpu_step(threads)
-        times.append(time.perf_counter() - t0)
-    sec = sum(times) / len(times)
-    units = getattr(wl, "cpu_units", wl.units())
-    value = units / sec / scale
-    sample = "full workload per step" if not hasattr(wl, "cpu_units") else "one (batch, head) of the workload per step"
+    sec, n = time_cpu(lambda: wl.cpu_step(threads), flush, args.warmup, args.steps, 1e9)
+    value = wl.cpu_units / sec / scale
     line = {"impl": "reference", "metric": metric, "value": round(value, 3), "unit": unit, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": str(wl.dtype).split(".")[-1],
             "data": "synthetic", "config": wl.config(1),
             "cpu_baseline": {"value": round(value, 3), "unit": unit, "cores": threads, "kind": "port",
-                             "sample": sample},
+                             "sample": f"{wl.cpu_sample}, median of {n} calls, caches flushed (2x LLC)"},
             "e2e": {"value": round(value, 3), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
@@ -520,6 +771,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="cfg2")
+    ap.add_argument("--also", default="cfg4,cfg5", help="comma-separated workloads recorded under 'also' ('' none)")
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -534,81 +786,29 @@ def main():
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        import datetime
-
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
 
-    wl = make_workload(args.workload, rank, world, dev)
-    stream = torch.cuda.current_stream(dev)
-    flush_buf = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
-    flush = lambda: flush_buf.fill_(1)  # noqa: E731
-    metric, unit, scale = metric_of(wl)
-
-    # clocks are sampled from here through the roofline and e2e phases: the
-    # whole window in which this run keeps the GPUs busy
-    barrier(world)
+    also = [w for w in args.also.split(",") if w and w != args.workload]
     sampler = ClockSampler(list(range(world))) if rank == 0 else None
     if sampler:
         sampler.start()
-    barrier(world)
-    step_ms = timed(wl.step, args.steps, args.warmup, flush, stream)
-    barrier(world)
-    total_ms = max_over_ranks(sum(step_ms), world)
-    units = sum_over_ranks(wl.units(), world)
-    ms_per_step = total_ms / args.steps
-    value = units / (ms_per_step * 1e-3) / scale
-
-    # the dominant kernel alone (roofline)
-    kern_ms = timed(wl.kernel_step, args.steps, 2, flush, stream)
-    kern_avg = statistics.mean(kern_ms)
-    pk, pk_kind = peaks()
-    if isinstance(wl, Prefill):
-        achieved = wl.kernel_units() / (kern_avg * 1e-3) / 1e12
-        peak, bound, runit = pk["bf16_tflops"], "tensor", "TFLOP/s"
-    else:
-        achieved = wl.kernel_units() / (kern_avg * 1e-3) / 1e9
-        peak, bound, runit = pk["hbm_gbs"], "hbm", "GB/s"
-    achieved = max_over_ranks(-achieved, world) * -1  # the slowest rank
-    roofline = {"bound": bound, "achieved": round(achieved, 2), "peak": peak, "peak_kind": pk_kind,
-                "unit": runit, "frac": round(achieved / peak, 4),
-                "traffic": TRAFFIC[args.workload][0] if args.workload in TRAFFIC else None,
-                "traffic_source": TRAFFIC[args.workload][1] if args.workload in TRAFFIC else None,
-                "kernel_ms": round(kern_avg, 4)}
-
-    # end to end through the public API, host buffers
-    wl.e2e_setup()
-    e2e_ms = timed(wl.e2e_step, args.steps, 2, flush, stream, hide_host=False)
-    e2e_total = max_over_ranks(sum(e2e_ms), world)
-    e2e_value = units / (e2e_total / args.steps * 1e-3) / scale
-
-    # N > 1 decode: the same step with the output all-gather after it
-    with_gather = None
-    if world > 1 and hasattr(wl, "gather_step"):
-        g_ms = timed(wl.gather_step, args.steps, 2, flush, stream)
-        g_total = max_over_ranks(sum(g_ms), world)
-        with_gather = {"value": round(units / (g_total / args.steps * 1e-3) / scale, 3), "unit": unit,
-                       "ms_per_step": round(g_total / args.steps, 4), "collective": "all_gather_into_tensor"}
-    barrier(world)
-    clocks = sampler.stop() if sampler else None
-
-    line = {"metric": metric, "value": round(value, 3), "unit": unit, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "us_per_call": round(ms_per_step * 1e3, 2),
-            "higher_is_better": True, "scaling": "strong" if getattr(wl, "engine", False) else "weak",
-            "vs_baseline": None, "dtype": str(wl.dtype).split(".")[-1], "data": "synthetic",
-            "config": wl.config(world), "roofline": roofline,
-            "e2e": {"value": round(e2e_value, 3), "unit": unit, "h2d_bytes_per_step": wl.h2d_bytes,
-                    "d2h_bytes_per_step": wl.d2h_bytes, "ms_per_step": round(e2e_total / args.steps, 4)},
-            "gpu_launches": wl.launches_per_step * args.steps, "clocks": clocks}
-    if with_gather is not None:
-        line["with_gather"] = with_gather
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        threads = os.cpu_count() or 1
-        sec, cunits, n = cpu_baseline(wl, threads)
-        sample = ("the full workload, median of %d calls" % n if not hasattr(wl, "cpu_units")
-                  else "one (batch, head) slice of the workload, median of %d calls" % n)
-        line["cpu_baseline"] = {"value": round(cunits / sec / scale, 4), "unit": unit, "cores": threads,
-                                "kind": "port", "sample": sample, "ms_per_call": round(sec * 1e3, 3)}
+    flush_host = HostFlush() if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
+    line = None
+    records = {}
+    for name in [args.workload] + also:
+        wl = make_workload(name, rank, world, dev)
+        rec = measure(wl, name, args, world, rank, sampler, flush_host)
+        if line is None:
+            line = rec
+        else:
+            records[name] = rec
+        del wl
+        torch.cuda.empty_cache()
+    if sampler:
+        sampler.stop()
+    if records:
+        line["also"] = records
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -46,6 +46,7 @@ SIGNATURES = {
     "ca_flash": (_I32, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _PI64, _PI64, _PI64, _F, _I32, _I32, _P,
                         _P]),
     "ca_status": (_I32, [_P, _I32, _P]),
+    "ca_set_wait_limit_ns": (None, [ctypes.c_uint64]),
     "ca_last_cuda_error": (ctypes.c_char_p, []),
     "ca_build_info": (ctypes.c_char_p, []),
 }

@@ -3,8 +3,8 @@
 // stream. Declarations and the contract live in include/cpu_attention_b200.h.
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cmath>
-#include <cstdlib>
 #include <cstdio>
 #include <mutex>
 #include <string>
@@ -17,6 +17,7 @@
 namespace {
 
 thread_local std::string g_cuda_error;
+std::atomic<uint64_t> g_wait_ns{0};  // 0: ca::kWaitLimitNs
 
 int cuda_fail(cudaError_t e, const char* what) {
   g_cuda_error = std::string(what) + ": " + cudaGetErrorString(e);
@@ -63,35 +64,24 @@ struct DecodePlan {
 constexpr int kDecodeRingTarget = 16384;  // bytes of ring per warp
 constexpr int kTasksPerSm = 32;           // split tasks per SM at most (task_cap / SMs)
 
-// CA_DECODE_STAGES / CA_DECODE_WARPS / CA_DECODE_PPW / CA_DECODE_AHEAD / CA_DECODE_TAILDIV override the plan (for
-// tuning sweeps); values that do not fit fall back to the defaults.
-int env_int(const char* name) {
-  const char* v = std::getenv(name);
-  return v ? std::atoi(v) : 0;
-}
-
 // Shared memory of the CTA-wide area behind the streaming warps' rings: the
 // task queue with its query rows, and the merge buffers.
 int decode_cta_extra(long long head_dim, int warps) { return ca::decode_cta_bytes((int)head_dim, warps); }
 
 bool decode_plan(long long head_dim, long long page, int dtype, const DeviceInfo& dev, DecodePlan* pl) {
   if (page > ca::kDecodeMaxPage) return false;
-  static const int o_st = env_int("CA_DECODE_STAGES"), o_w = env_int("CA_DECODE_WARPS"),
-                   o_ppw = env_int("CA_DECODE_PPW"), o_ah = env_int("CA_DECODE_AHEAD"), o_td = env_int("CA_DECODE_TAILDIV");
   const long long page_bytes = page * head_dim * (long long)elem_size(dtype);
   pl->page_bytes = (int)page_bytes;
   pl->kslot_bytes = (int)page_bytes + ca::kKSlotPadBytes;
   pl->stage_bytes = pl->kslot_bytes + (int)page_bytes;
   const int budget = dev.max_smem_optin - 1024;
   int stages = std::max(2, std::min(4, kDecodeRingTarget / pl->stage_bytes));
-  if (o_st >= 2 && o_st <= 8) stages = o_st;
   auto warp_bytes = [&](int s) { return ca::decode_warp_bytes(s, pl->stage_bytes); };
   auto fits = [&](int s, int warps) { return warps * warp_bytes(s) + decode_cta_extra(head_dim, warps) <= budget; };
   while (stages > 2 && !fits(stages, 1)) --stages;
   if (!fits(stages, 1)) return false;
   int warps = ca::kDecodeMaxWarps;
   while (warps > 1 && !fits(stages, warps)) --warps;
-  if (o_w > 0 && o_w < warps) warps = o_w;
   pl->stages = stages;
   pl->warps = warps;
   pl->warp_bytes = warp_bytes(stages);
@@ -99,10 +89,12 @@ bool decode_plan(long long head_dim, long long page, int dtype, const DeviceInfo
   pl->ctas = dev.sms;
   // task unit: 5 pages per streaming warp (measured 1.5% faster than 4 on the
   // ragged cfg2 workload, equal on the others)
-  pl->pages_per_warp = (o_ppw > 0 && o_ppw <= 64) ? o_ppw : 5;
+  pl->pages_per_warp = 5;
   pl->task_cap = kTasksPerSm * dev.sms;
-  pl->ahead = (o_ah > 0 && o_ah <= 4096) ? o_ah : ca::kDecodeAhead;
-  pl->tail_div = (o_td > 0 && o_td <= 16) ? o_td : 2;
+  pl->ahead = ca::kDecodeAhead;
+  // the last tasks are half the size of the others (a third: +3% and -1% on
+  // cfg2 in two sweeps, -1.5% on the E=32 cross-attention case)
+  pl->tail_div = 2;
   return true;
 }
 
@@ -321,6 +313,8 @@ int decode_impl(const void* q, int64_t q_stride, void* k_cache, void* v_cache, i
   prm.partial = partial;
   prm.tickets = tickets;
   prm.status = status;
+  const uint64_t wl = g_wait_ns.load();
+  prm.wait_ns = wl ? wl : ca::kWaitLimitNs;
   if (dtype == CA_DTYPE_BF16) return dispatch_decode<__nv_bfloat16>(head_dim, prm, pl, s, device);
   return dispatch_decode<float>(head_dim, prm, pl, s, device);
 }
@@ -388,18 +382,31 @@ int ca_flash(const void* q, const void* k, const void* v, void* out, int64_t bat
 
 int ca_status(void* workspace, int reset, void* stream) {
   if (!workspace) return CA_ENULL;
-  int32_t host = 0;
+  // words: status, task counter, and the last decode launch's ticket count and
+  // byte offset (written by that launch)
+  int32_t host[4] = {0, 0, 0, 0};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t e = cudaMemcpyAsync(&host, workspace, 4, cudaMemcpyDeviceToHost, s);
+  cudaError_t e = cudaMemcpyAsync(host, workspace, sizeof(host), cudaMemcpyDeviceToHost, s);
   if (e != cudaSuccess) return cuda_fail(e, "status read");
-  if (reset) {
-    e = cudaMemsetAsync(workspace, 0, 4, s);
-    if (e != cudaSuccess) return cuda_fail(e, "status reset");
-  }
   e = cudaStreamSynchronize(s);
   if (e != cudaSuccess) return cuda_fail(e, "status sync");
-  return host;
+  if (reset) {
+    char* ws = static_cast<char*>(workspace);
+    e = cudaMemsetAsync(ws, 0, 4, s);
+    // A timed-out decode leaves the tasks it abandoned counted and their
+    // items' tickets short of complete: clear the counter and the tickets, or
+    // the next call on this workspace would leave those rows unwritten.
+    if (e == cudaSuccess && (host[0] & CA_STATUS_TIMEOUT)) {
+      e = cudaMemsetAsync(ws + 4, 0, 4, s);
+      if (e == cudaSuccess && host[2] > 0 && host[3] >= 256)
+        e = cudaMemsetAsync(ws + host[3], 0, (size_t)host[2] * 4, s);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "status reset");
+  }
+  return host[0];
 }
+
+void ca_set_wait_limit_ns(uint64_t ns) { g_wait_ns.store(ns); }
 
 const char* ca_last_cuda_error(void) { return g_cuda_error.c_str(); }
 

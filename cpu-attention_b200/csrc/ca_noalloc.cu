@@ -28,7 +28,9 @@
 // Set-up: the first call on each device, with that device current, looks up
 // the array's device address (cudaGetSymbolAddress; in host code the array's
 // name is only a host-side stand-in). Make that first call before any stream
-// capture.
+// capture. The address is kept until the process exits, so resetting the
+// device (cudaDeviceReset) after that first call is not supported: the module
+// would be loaded again at another address.
 #include <cuda_runtime.h>
 
 #include <mutex>

@@ -109,8 +109,9 @@ struct DecodeParams {
   int task_cap;        // tasks of split items number at most 2 * task_cap
   float* partial;      // [2 * task_cap + 2][E + 2]
   int* tickets;        // [B * H], zero between calls
-  int* status;         // CA_STATUS_* bits
+  int* status;         // CA_STATUS_* bits; status[2], status[3]: this call's ticket count and byte offset
   int* counter;        // tasks handed out, zero between calls
+  unsigned long long wait_ns;  // limit of each bounded wait on another warp or a copy
 };
 
 // Attended length of sequence i (clamped, and flagged, when it exceeds the
@@ -211,12 +212,12 @@ struct DecodeTile {
 };
 
 // Bounded wait that also returns at once when this CTA already gave up.
-__device__ __forceinline__ bool decode_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+__device__ __forceinline__ bool decode_wait(uint64_t* bar, uint32_t parity, volatile int* abort, uint64_t limit) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 0 && (*abort || global_timer_ns() - t0 > kWaitLimitNs)) return false;
+    if ((it & 255u) == 0 && (*abort || global_timer_ns() - t0 > limit)) return false;
   }
 }
 
@@ -260,14 +261,14 @@ __host__ __device__ constexpr int decode_warp_bytes(int stages, int stage_bytes)
   return (stages * stage_bytes + kDecodeMaxPage * 4 + stages * 8 + stages * 16 + 127) / 128 * 128;
 }
 
-// Spins until `ok()` (bounded; false on timeout or abort).
+// Spins until `ok()` (bounded by `limit` ns; false on timeout or abort).
 template <typename F>
-__device__ __forceinline__ bool spin_until(F ok, volatile int* abort) {
+__device__ __forceinline__ bool spin_until(F ok, volatile int* abort, uint64_t limit) {
   if (ok()) return true;
   const uint64_t t0 = global_timer_ns();
   for (uint32_t it = 1;; ++it) {
     if (ok()) return true;
-    if ((it & 63u) == 0 && (*abort || global_timer_ns() - t0 > kWaitLimitNs)) return false;
+    if ((it & 63u) == 0 && (*abort || global_timer_ns() - t0 > limit)) return false;
     __nanosleep(kSpinSleepNs);
   }
 }
@@ -315,6 +316,11 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
 
   if (w == W + 1) {
     // ================================================================= feeder
+    // the call's ticket range, for the host to clear after a timeout (ca_status)
+    if (blockIdx.x == 0 && lane == 0) {
+      p.status[2] = p.B * p.H;
+      p.status[3] = (int)(reinterpret_cast<char*>(p.tickets) - reinterpret_cast<char*>(p.status));
+    }
     // ---- plan: task sizes and the number of tasks (only the feeder needs
     // them; the other warps go straight to their roles). The pages of the
     // first kPlanRegs * 32 sequences are read once and kept in registers for
@@ -459,7 +465,7 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
     for (int qg = 0;; ++qg) {
       if (!staged) {
         // near the end of the pool: grab only once this CTA needs the task
-        if (!spin_until([&] { return qg - *sMerged < QD && published - *(volatile int*)sNext < p.ahead; }, sAbort)) {
+        if (!spin_until([&] { return qg - *sMerged < QD && published - *(volatile int*)sNext < p.ahead; }, sAbort, p.wait_ns)) {
           give_up();
           break;
         }
@@ -471,7 +477,7 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
       if (!spin_until([&] {
             return qg - *sMerged < QD && published - *(volatile int*)sNext < p.ahead &&
                    (!fast || published + sn - *sMergedPages <= kDecodeBlkRing);
-          }, sAbort)) {
+          }, sAbort, p.wait_ns)) {
         give_up();
         break;
       }
@@ -568,7 +574,7 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
     bool ok = true;
     for (int q = 0; ok; ++q) {
       const int r = q % QD;
-      if (!spin_until([&] { return sSeq[r] == q; }, sAbort)) {
+      if (!spin_until([&] { return sSeq[r] == q; }, sAbort, p.wait_ns)) {
         ok = false;
         break;
       }
@@ -581,7 +587,7 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
       float M = -INFINITY, L = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
       for (int gg = est; gg < est + en; ++gg) {
         const int ps = gg % R;
-        if (!spin_until([&] { return sFlag[ps] == gg; }, sAbort)) {
+        if (!spin_until([&] { return sFlag[ps] == gg; }, sAbort, p.wait_ns)) {
           ok = false;
           break;
         }
@@ -618,7 +624,7 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
       }
       // ---- a split task: to the finisher
       const int fr = nf % FQ;
-      if (!spin_until([&] { return nf < FQ || sFinAck[fr] == nf - FQ; }, sAbort)) {
+      if (!spin_until([&] { return nf < FQ || sFinAck[fr] == nf - FQ; }, sAbort, p.wait_ns)) {
         ok = false;
         break;
       }
@@ -644,7 +650,7 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
     // an end marker for each finisher (they also stop on abort)
     for (int k = 0; k < kDecodeFinishers; ++k, ++nf) {
       const int fr = nf % FQ;
-      if (!spin_until([&] { return nf < FQ || sFinAck[fr] == nf - FQ; }, sAbort)) break;
+      if (!spin_until([&] { return nf < FQ || sFinAck[fr] == nf - FQ; }, sAbort, p.wait_ns)) break;
       if (lane == 0) {
         sFe[fr].i = -1;
         __threadfence_block();
@@ -663,7 +669,7 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
     T* obase = static_cast<T*>(p.out);
     for (int f = w - (W + 2);; f += kDecodeFinishers) {
       const int fr = f % FQ;
-      if (!spin_until([&] { return sFin[fr] == f; }, sAbort)) break;
+      if (!spin_until([&] { return sFin[fr] == f; }, sAbort, p.wait_ns)) break;
       __threadfence_block();
       const int ei = sFe[fr].i;
       if (ei < 0) break;
@@ -819,7 +825,7 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
       if (!spin_until([&] {
             produce();
             return pidx != cidx || pdone;
-          }, sAbort)) {
+          }, sAbort, p.wait_ns)) {
         failed = true;
         fail_idx = cidx;
         break;
@@ -844,7 +850,7 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
     float m, lpart = 0.f;
     {
       const uint32_t parity = (cidx / (unsigned)p.stages) & 1u;
-      if (!decode_wait(&sBar[s], parity, sAbort)) {
+      if (!decode_wait(&sBar[s], parity, sAbort, p.wait_ns)) {
         failed = true;
         fail_idx = cidx;
         break;
@@ -1003,7 +1009,7 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
       for (int cc = 0; cc < 4; ++cc) acc[cc] += __shfl_xor_sync(0xffffffffu, acc[cc], o);
     }
     const int gz = tag.z;
-    if (!spin_until([&] { return *sMergedPages > gz - R; }, sAbort)) {
+    if (!spin_until([&] { return *sMergedPages > gz - R; }, sAbort, p.wait_ns)) {
       failed = true;
       fail_idx = cidx;
       break;

@@ -29,6 +29,28 @@ struct FlashParams {
   int causal;
 };
 
+// The (query block, head, batch) of a CTA of a 1-D prefill grid of
+// nblk * heads * batch CTAs (launched in index order). Causal grids run in
+// longest-processing-time order: the query block is the slowest index and
+// descending, so every (batch, head)'s heaviest block goes first and the grid
+// ends on the one-tile blocks, which keeps SMs from idling behind a late heavy
+// block. Non-causal grids keep a (batch, head)'s blocks adjacent (they share
+// its K/V through L2).
+__device__ __forceinline__ void flash_block_of(int lin, int nblk, int heads, bool causal, int* blk, int* h, int* b) {
+  if (causal) {
+    const int nhb = (int)(gridDim.x / (unsigned)nblk);
+    *blk = nblk - 1 - lin / nhb;
+    const int pair = lin % nhb;
+    *h = pair % heads;
+    *b = pair / heads;
+  } else {
+    *blk = lin % nblk;
+    const int pair = lin / nblk;
+    *h = pair % heads;
+    *b = pair / heads;
+  }
+}
+
 namespace generic {
 constexpr int BQ = 64;  // query rows per CTA
 constexpr int BK = 64;  // keys per tile
@@ -46,16 +68,8 @@ __global__ void __launch_bounds__(128) flash_generic_kernel(const __grid_constan
   float* sQ = sV + BK * E;       // [BQ][E]
   float* sP = sQ + BQ * E;       // [4 warps][BK][RW]  (key-major: 4 rows per float4)
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  // Causal: heaviest query blocks of every (batch, head) launch first (the
-  // linear block index maps to a descending query block, slowest).
-  int blk = (int)blockIdx.x, h = (int)blockIdx.y, b = (int)blockIdx.z;
-  if (p.causal) {
-    const int nhb = (int)(gridDim.y * gridDim.z);
-    const int lin = (int)(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z));
-    blk = (int)gridDim.x - 1 - lin / nhb;
-    h = (lin % nhb) % (int)gridDim.y;
-    b = (lin % nhb) / (int)gridDim.y;
-  }
+  int blk, h, b;
+  flash_block_of((int)blockIdx.x, (p.Lq + BQ - 1) / BQ, p.H, p.causal != 0, &blk, &h, &b);
   const int q0 = blk * BQ;
   const T* qg = static_cast<const T*>(p.q) + b * p.qs[0] + h * p.qs[2];
   const T* kg = static_cast<const T*>(p.k) + b * p.ks[0] + h * p.ks[2];
@@ -188,22 +202,31 @@ inline size_t flash_generic_smem(int E) {
   return sizeof(float) * ((size_t)E * KP + (size_t)BK * E + (size_t)BQ * E + 4 * (size_t)BK * RW);
 }
 
+// Raises a kernel's dynamic shared memory limit to `smem` on the current
+// device, once per device (`done` is the kernel's own per-device record).
+inline cudaError_t smem_limit_once(const void* kern, int smem, unsigned char (&done)[64]) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) return e != cudaSuccess ? e : cudaErrorInvalidDevice;
+  if (done[dev]) return cudaSuccess;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e == cudaSuccess) done[dev] = 1;  // (a race sets the same value twice)
+  return e;
+}
+
 template <typename T, int E>
 int flash_generic_launch(const FlashParams& p, cudaStream_t stream, std::string* err) {
   const size_t smem = flash_generic_smem(E);
-  static bool configured = false;  // attribute is per function; benign race sets the same value
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(flash_generic_kernel<T, E>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
-    if (e != cudaSuccess) {
-      *err = std::string("cudaFuncSetAttribute(flash): ") + cudaGetErrorString(e);
-      return CA_ECUDA;
-    }
-    configured = true;
+  static unsigned char configured[64] = {0};
+  cudaError_t e = smem_limit_once(reinterpret_cast<const void*>(flash_generic_kernel<T, E>), (int)smem, configured);
+  if (e != cudaSuccess) {
+    *err = std::string("cudaFuncSetAttribute(flash): ") + cudaGetErrorString(e);
+    return CA_ECUDA;
   }
-  dim3 grid((p.Lq + generic::BQ - 1) / generic::BQ, p.H, p.B);
-  flash_generic_kernel<T, E><<<grid, 128, smem, stream>>>(p);
-  cudaError_t e = cudaGetLastError();
+  const long long ctas = (long long)((p.Lq + generic::BQ - 1) / generic::BQ) * p.H * p.B;
+  if (ctas > 0x7fffffffLL) return CA_EUNSUPPORTED;
+  flash_generic_kernel<T, E><<<(unsigned)ctas, 128, smem, stream>>>(p);
+  e = cudaGetLastError();
   if (e != cudaSuccess) {
     *err = std::string("flash launch: ") + cudaGetErrorString(e);
     return CA_ECUDA;

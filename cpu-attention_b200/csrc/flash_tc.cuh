@@ -32,6 +32,7 @@
 
 #include <type_traits>
 
+#include "flash.cuh"
 #include "tcgen05.cuh"
 
 namespace ca {
@@ -157,19 +158,8 @@ __global__ void __launch_bounds__(384, 1) flash_tc_kernel(const __grid_constant_
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nblk = (a.Lq + C::ROWS - 1) / C::ROWS;
-  // Causal: CTAs are launched in linear block order, so the linear index is
-  // mapped to (query block, head, batch) with the query block slowest and
-  // descending: every (batch, head)'s heaviest block goes first and the grid
-  // ends on the one-tile blocks (longest-processing-time order, which keeps
-  // SMs from idling behind a late heavy block).
-  int blk = (int)blockIdx.x, h = (int)blockIdx.y, b = (int)blockIdx.z;
-  if (CAUSAL) {
-    const int nhb = (int)(gridDim.y * gridDim.z);
-    const int lin = (int)(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z));
-    blk = nblk - 1 - lin / nhb;
-    h = (lin % nhb) % (int)gridDim.y;
-    b = (lin % nhb) / (int)gridDim.y;
-  }
+  int blk, h, b;
+  flash_block_of((int)blockIdx.x, nblk, a.H, CAUSAL, &blk, &h, &b);
   const int q0 = blk * C::ROWS;
   const int nt0 = tc_tiles(q0, a.Lq, a.Lk, CAUSAL), nt1 = tc_tiles(q0 + C::BM, a.Lq, a.Lk, CAUSAL);
   const int nt = max(nt0, nt1);
@@ -519,23 +509,26 @@ int flash_tc_launch(const FlashParams& p, int* status, cudaStream_t stream, std:
   a.c = p.c;
   a.causal = p.causal;
   a.status = status;
-  static bool configured[2] = {false, false};
+  static unsigned char configured[2][64] = {};
+  static int regs_ok[2] = {0, 0};  // 0: not checked, 1: as planned, -1: not
   auto kern = p.causal ? flash_tc_kernel<E, true> : flash_tc_kernel<E, false>;
-  if (!configured[p.causal]) {
+  if (regs_ok[p.causal] == 0) {
     // the register split assumes exactly REGS_LAUNCH registers per thread at
     // launch (a larger split would wait forever in setmaxnreg)
     cudaFuncAttributes fa;
-    if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess || fa.numRegs != C::REGS_LAUNCH) return CA_EUNSUPPORTED;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
-    if (e != cudaSuccess) {
-      *err = std::string("cudaFuncSetAttribute(flash_tc): ") + cudaGetErrorString(e);
-      return CA_ECUDA;
-    }
-    configured[p.causal] = true;
+    if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) return CA_EUNSUPPORTED;
+    regs_ok[p.causal] = fa.numRegs == C::REGS_LAUNCH ? 1 : -1;
   }
-  dim3 grid((p.Lq + C::ROWS - 1) / C::ROWS, p.H, p.B);
-  kern<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(a);
-  cudaError_t e = cudaGetLastError();
+  if (regs_ok[p.causal] < 0) return CA_EUNSUPPORTED;
+  cudaError_t e = smem_limit_once(reinterpret_cast<const void*>(kern), C::SMEM_BYTES, configured[p.causal]);
+  if (e != cudaSuccess) {
+    *err = std::string("cudaFuncSetAttribute(flash_tc): ") + cudaGetErrorString(e);
+    return CA_ECUDA;
+  }
+  const long long ctas = (long long)((p.Lq + C::ROWS - 1) / C::ROWS) * p.H * p.B;
+  if (ctas > 0x7fffffffLL) return CA_EUNSUPPORTED;
+  kern<<<(unsigned)ctas, C::THREADS, C::SMEM_BYTES, stream>>>(a);
+  e = cudaGetLastError();
   if (e != cudaSuccess) {
     *err = std::string("flash_tc launch: ") + cudaGetErrorString(e);
     return CA_ECUDA;

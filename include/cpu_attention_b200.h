@@ -113,7 +113,7 @@ CA_API int ca_decode(const void* q, int64_t q_stride, void* k_cache, void* v_cac
  * Replaces the reference's two-step path for k/v holding several new tokens
  * per sequence (`flash_attn_interface.py:109-117`: the tokens are stored at
  * cache_seqlens + j by `reshape_and_cache`, then `_C.decode` attends the grown
- * cache), §8(f) rank 1 of the hot path: here the decode launch itself writes
+ * cache). Here the decode launch itself writes
  * the tokens (the warp that streams a page holding new tokens patches them in
  * and writes them to the cache) and attends lens[i] + n_new keys.
  * k_new/v_new: token j of sequence i at element i * kv_stride +
@@ -143,7 +143,8 @@ CA_API int ca_decode_append(const void* q, int64_t q_stride, void* k_cache,
  * Every call shares the array: calls that overlap on the GPU race; order them.
  *   Device-found value errors are skipped but not reported (validate on the
  *   host). The first call on a device looks up the array's address; make it
- *   before any stream capture.
+ *   before any stream capture. The address is kept for the life of the
+ *   process: a cudaDeviceReset after that first call is not supported.
  */
 CA_API int ca_decode_noalloc(const void* q, int64_t q_stride, void* k_cache,
               void* v_cache, int64_t num_blocks, const void* k_new,
@@ -177,9 +178,18 @@ CA_API int ca_flash(const void* q, const void* k, const void* v, void* out,
 
 /* ---- runtime ------------------------------------------------------------ */
 /* The status word of a decode workspace (ORed CA_STATUS_* bits since the last
- * reset); synchronises `stream`. reset != 0 clears it. Returns < 0 on a CUDA
- * error. */
+ * reset); synchronises `stream`. reset != 0 clears it; when the word holds
+ * CA_STATUS_TIMEOUT it also clears what a decode that gave up leaves behind
+ * (its task counter and the tickets of its (sequence, head) items), so the
+ * workspace serves the next call again. Returns < 0 on a CUDA error. */
 CA_API int ca_status(void* workspace, int reset, void* stream);
+
+/* The limit of each bounded device wait of the decode kernels from the next
+ * call on (process-wide), in nanoseconds; 0 restores the default of 2 s. No
+ * counterpart in the reference: it exists so that failure handling can be
+ * tested (a wait that runs out sets CA_STATUS_TIMEOUT and the kernel returns)
+ * without faulting or hanging a GPU. */
+CA_API void ca_set_wait_limit_ns(uint64_t ns);
 
 /* The last CUDA error string seen by this library on this host thread. */
 CA_API const char* ca_last_cuda_error(void);
