@@ -2,10 +2,11 @@
 
     python cpu-attention_b200/build.py [--force] [--verbose]
 
-One nvcc invocation: csrc/ca_abi.cu (which includes every kernel) and
-csrc/ca_noalloc.cu (the allocation-free decode entry) ->
-cpu_attention/libca_b200.so, compiled for sm_100a only, with line info, static
-CUDA runtime. Rebuilds only when a source or this script is newer than the
+One nvcc process per translation unit, in parallel: csrc/ca_abi.cu (the C ABI,
+the store and prefill kernels), csrc/decode_bf16.cu and csrc/decode_f32.cu (the
+decode kernel's instantiations) and csrc/ca_noalloc.cu (the allocation-free
+decode entry), objects under cpu-attention_b200/_build/, linked into
+cpu_attention/libca_b200.so; sm_100a only, with line info, static CUDA runtime. Rebuilds only when a source or this script is newer than the
 library. nvcc cross-compiles, so this runs on a machine without a GPU.
 """
 
@@ -46,16 +47,33 @@ def stale():
     return any(os.path.getmtime(f) > t for f in sources())
 
 
+UNITS = ["ca_abi.cu", "ca_noalloc.cu", "decode_bf16.cu", "decode_f32.cu"]
+
+
 def build(force=False, verbose=False):
-    """Compile the library if needed; returns its path."""
+    """Compile the library if needed; returns its path. Each translation unit
+    compiles in its own nvcc process (in parallel), then one link."""
     if not force and not stale():
         return OUT
+    from concurrent.futures import ThreadPoolExecutor
+
+    objdir = os.path.join(HERE, "_build")
+    os.makedirs(objdir, exist_ok=True)
+    flags = [f for f in FLAGS if f != "-shared"]
+
+    def compile_unit(unit):
+        obj = os.path.join(objdir, unit.replace(".cu", ".o"))
+        cmd = [nvcc(), *ARCH, *flags, "-c", "-o", obj, os.path.join(CSRC, unit)]
+        if verbose:
+            cmd.insert(1, "-Xptxas=-v")
+            print(" ".join(cmd), flush=True)
+        subprocess.run(cmd, check=True)
+        return obj
+
+    with ThreadPoolExecutor(max_workers=len(UNITS)) as pool:
+        objs = list(pool.map(compile_unit, UNITS))
     tmp = OUT + ".tmp"
-    cmd = [nvcc(), *ARCH, *FLAGS, "-o", tmp, os.path.join(CSRC, "ca_abi.cu"), os.path.join(CSRC, "ca_noalloc.cu")]
-    if verbose:
-        cmd.insert(1, "-Xptxas=-v")
-        print(" ".join(cmd), flush=True)
-    subprocess.run(cmd, check=True)
+    subprocess.run([nvcc(), *ARCH, "-shared", "-o", tmp, *objs], check=True)
     os.replace(tmp, OUT)
     return OUT
 

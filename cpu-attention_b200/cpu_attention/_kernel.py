@@ -41,6 +41,10 @@ SIGNATURES = {
                          _I64, _I64, _I64, _I64, _I32, _F, _P, _SZ, _P]),
     "ca_decode_append": (_I32, [_P, _I64, _P, _P, _I64, _P, _P, _I64, _I64, _I64, _P, _P, _I64, _P,
                                 _I64, _I64, _I64, _I64, _I32, _F, _P, _SZ, _P]),
+    "ca_decode_ex": (_I32, [_P, _I64, _P, _P, _I64, _P, _P, _I64, _I64, _I64, _P, _P, _P, _I64, _P, _P,
+                            _I64, _I64, _I64, _I64, _I64, _I32, _F, _P, _SZ, _P]),
+    "ca_flash_ex": (_I32, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _PI64, _PI64, _PI64, _P, _P,
+                           _I64, _I64, _F, _I32, _I32, _P, _P]),
     "ca_decode_noalloc": (_I32, [_P, _I64, _P, _P, _I64, _P, _P, _I64, _P, _P, _P, _I64, _P,
                                  _I64, _I64, _I64, _I64, _I32, _F, _P]),
     "ca_flash": (_I32, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _PI64, _PI64, _PI64, _F, _I32, _I32, _P,

@@ -74,23 +74,33 @@ def _scale(scale):
     return float("nan") if scale is None else float(scale)
 
 
-def decode(rt, q, k_cache, v_cache, k, v, slots, lens, page_table, scale, dst):
-    """Paged decode of q ``[seqs, (1,) heads, dim]`` (MHA). With k/v, each
+def _lse_ok(lse, shape, dev):
+    return (lse is None or (isinstance(lse, torch.Tensor) and lse.dtype == torch.float32 and lse.is_cuda
+                            and lse.get_device() == dev.index and tuple(lse.shape) == shape
+                            and lse.is_contiguous()))
+
+
+def decode(rt, q, k_cache, v_cache, k, v, slots, lens, page_table, scale, dst, lse=None):
+    """Paged decode of q ``[seqs, (1,) heads, dim]`` against caches of
+    ``kv_heads`` heads (``heads % kv_heads == 0``: query head h reads KV head
+    ``h // (heads // kv_heads)``). With k/v (``kv_heads`` heads), each
     sequence's new token is stored first: at ``slots`` (then ``lens`` is the
     length after the store), or appended at ``lens`` (the length before). k/v
-    of shape ``[seqs, n, heads, dim]`` with n > 1 append n tokens at ``lens``
-    in the same launch (``ca_decode_append``). Writes ``dst`` when given, else a
-    new tensor; returns it, or None (`_C.mojo:87-171`)."""
+    of shape ``[seqs, n, kv_heads, dim]`` with n > 1 append n tokens at
+    ``lens`` in the same launch. Writes ``dst`` when given, else a new tensor,
+    and each row's log-sum-exp into ``lse`` (float32 ``[seqs, heads]``) when
+    given; returns the output, or None (`_C.mojo:87-171`)."""
     del rt
     fast = K.fastpath()
-    if fast is not None and _plain_tensors(q, k_cache, v_cache, lens, page_table) and _plain_or_none(k, v, slots, dst):
+    if (fast is not None and _plain_tensors(q, k_cache, v_cache, lens, page_table)
+            and _plain_or_none(k, v, slots, dst, lse)):
         # the same checks and call in C++ (cpu_attention/_fastpath)
         out = fast.decode(q, k_cache, v_cache, k, v, slots, lens, page_table, None if scale is None else float(scale),
-                          dst)
+                          dst, lse)
         if out is not None and K.CHECK:
             K.raise_status(out.device, K.current_stream(out.device))
         return out
-    dev = _cuda(q, k_cache, v_cache, k, v, slots, lens, page_table, dst)
+    dev = _cuda(q, k_cache, v_cache, k, v, slots, lens, page_table, dst, lse)
     if dev is None or not isinstance(q, torch.Tensor):
         return None
     nd = q.dim()
@@ -98,9 +108,10 @@ def decode(rt, q, k_cache, v_cache, k, v, slots, lens, page_table, scale, dst):
         return None
     b, heads, hd = q.shape[0], q.shape[-2], q.shape[-1]
     dt = K.DTYPES.get(q.dtype)
-    if dt is None or hd not in K.HEAD_DIMS or not _rows_ok(q, hd):
+    if dt is None or hd not in K.HEAD_DIMS or not _rows_ok(q, hd) or k_cache.dim() != 4:
         return None
-    if not _caches_ok(k_cache, v_cache, q.dtype, heads, hd):
+    kvh = k_cache.shape[1]
+    if kvh < 1 or heads % kvh or not _caches_ok(k_cache, v_cache, q.dtype, kvh, hd):
         return None
     page = k_cache.shape[2]
     if (page_table.dim() != 2 or page_table.dtype != torch.int32 or page_table.shape[0] != b
@@ -109,19 +120,20 @@ def decode(rt, q, k_cache, v_cache, k, v, slots, lens, page_table, scale, dst):
     if not _int_vector(lens, torch.int32, b):
         return None
     store = k is not None
-    n_new = 1
+    n_new = 0
     if store:
-        multi = (nd == 4 and slots is None and k.dim() == 4 and k.shape[0] == b and k.shape[1] > 1
-                 and tuple(k.shape[2:]) == (heads, hd))
-        if v is None or (k.shape != q.shape and not multi) or v.shape != k.shape or v.stride() != k.stride():
+        if v is None or k.dim() != nd or v.shape != k.shape or v.stride() != k.stride():
             return None
-        if k.dtype != q.dtype or v.dtype != q.dtype or not _rows_ok(k, hd):
+        if k.shape[0] != b or tuple(k.shape[-2:]) != (kvh, hd) or (nd == 4 and k.shape[1] < 1):
             return None
-        if multi:
-            n_new = k.shape[1]
+        n_new = k.shape[1] if nd == 4 else 1
+        if k.dtype != q.dtype or v.dtype != q.dtype or not _rows_ok(k, hd) or (slots is not None and n_new != 1):
+            return None
     elif v is not None:
         return None
     if slots is not None and not (store and _int_vector(slots, torch.int64, b)):
+        return None
+    if not _lse_ok(lse, (b, heads), dev):
         return None
     if dst is None:
         out = torch.empty(q.shape, dtype=q.dtype, device=dev)
@@ -138,19 +150,13 @@ def decode(rt, q, k_cache, v_cache, k, v, slots, lens, page_table, scale, dst):
         return None
     ws = K.workspace(dev, stream, need)
     with K.on_device(dev):
-        if n_new > 1:
-            rc = lib.ca_decode_append(
-                q.data_ptr(), q.stride(0), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.shape[0],
-                k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1), n_new, lens.data_ptr(),
-                page_table.data_ptr(), page_table.shape[1], out.data_ptr(), b, heads, hd, page, dt,
-                _scale(scale), ws.data_ptr(), ws.numel(), stream)
-        else:
-            rc = lib.ca_decode(
-                q.data_ptr(), q.stride(0), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.shape[0],
-                k.data_ptr() if store else None, v.data_ptr() if store else None, k.stride(0) if store else 0,
-                slots.data_ptr() if slots is not None else None, lens.data_ptr(), page_table.data_ptr(),
-                page_table.shape[1], out.data_ptr(), b, heads, hd, page, dt, _scale(scale), ws.data_ptr(),
-                ws.numel(), stream)
+        rc = lib.ca_decode_ex(
+            q.data_ptr(), q.stride(0), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.shape[0],
+            k.data_ptr() if store else None, v.data_ptr() if store else None, k.stride(0) if store else 0,
+            k.stride(1) if store and nd == 4 else 0, n_new, slots.data_ptr() if slots is not None else None,
+            lens.data_ptr(), page_table.data_ptr(), page_table.shape[1], out.data_ptr(),
+            lse.data_ptr() if lse is not None else None, b, heads, kvh, hd, page, dt, _scale(scale), ws.data_ptr(),
+            ws.numel(), stream)
     if not _check_rc(rc):
         return None
     if K.CHECK:
@@ -189,40 +195,69 @@ def store(rt, key, value, k_cache, v_cache, slots):
     return True
 
 
-def flash(rt, q, k, v, scale, causal):
-    """flash_attn_func over q/k/v ``[batch, seq, heads, dim]`` (MHA, dims
-    contiguous). Returns the output, or None (`_C.mojo:232-316`)."""
+def flash(rt, q, k, v, scale, causal, lse=None, cu_q=None, cu_k=None, max_q=None, max_k=None):
+    """flash_attn_func over q ``[batch, seq, heads, dim]`` and k/v ``[batch,
+    seq_k, kv_heads, dim]`` (``heads % kv_heads == 0``; dims contiguous), or,
+    with ``cu_q``/``cu_k`` (int32 ``[batch + 1]`` token offsets) and the
+    largest lengths ``max_q``/``max_k``, over packed q ``[total_q, heads,
+    dim]`` and k/v ``[total_k, kv_heads, dim]``. Each row's log-sum-exp goes to
+    ``lse`` (float32 ``[batch, heads, seq]``, or ``[heads, total_q]`` packed)
+    when given. Returns the output, or None (`_C.mojo:232-316`)."""
     del rt
+    var = cu_q is not None or cu_k is not None
     fast = K.fastpath()
-    if fast is not None and _plain_tensors(q, k, v) and (causal is True or causal is False):
+    if (not var and lse is None and fast is not None and _plain_tensors(q, k, v)
+            and (causal is True or causal is False)):
         # the same checks and call in C++ (cpu_attention/_fastpath)
         out = fast.flash(q, k, v, None if scale is None else float(scale), causal)
         if out is not None and K.CHECK:
             K.raise_status(out.device, K.current_stream(out.device))
         return out
-    dev = _cuda(q, k, v)
-    if dev is None or q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
+    dev = _cuda(q, k, v, lse, cu_q, cu_k)
+    if dev is None or causal is not True and causal is not False:
         return None
-    b, sq, heads, hd = q.shape
-    sk = k.shape[1]
+    nd = 3 if var else 4
+    if q.dim() != nd or k.dim() != nd or v.shape != k.shape:
+        return None
+    heads, hd, kvh = q.shape[-2], q.shape[-1], k.shape[-2]
     dt = K.DTYPES.get(q.dtype)
-    if dt is None or hd not in K.HEAD_DIMS or sq < 1 or sk < 1:
+    if dt is None or hd not in K.HEAD_DIMS or k.shape[-1] != hd or kvh < 1 or heads % kvh:
         return None
-    if k.shape[0] != b or k.shape[2] != heads or k.shape[3] != hd or k.dtype != q.dtype or v.dtype != q.dtype:
+    if k.dtype != q.dtype or v.dtype != q.dtype or q.stride(-1) != 1 or k.stride(-1) != 1 or v.stride(-1) != 1:
         return None
-    if v.shape != k.shape or q.stride(3) != 1 or k.stride(3) != 1 or v.stride(3) != 1:
+    if var:
+        if cu_q is None or cu_k is None or max_q is None or max_k is None:
+            return None
+        b = cu_q.shape[0] - 1
+        if b < 0 or not (_int_vector(cu_q, torch.int32, b + 1) and _int_vector(cu_k, torch.int32, b + 1)):
+            return None
+        sq, sk, tq, tk = int(max_q), int(max_k), q.shape[0], k.shape[0]
+        if sq < 1 or sk < 1:
+            return None
+        strides = [(0,) + tuple(x.stride()) for x in (q, k, v)]
+        lse_shape = (heads, tq)
+    else:
+        b, sq = q.shape[0], q.shape[1]
+        sk, tq, tk = k.shape[1], 0, 0
+        if sq < 1 or sk < 1 or k.shape[0] != b:
+            return None
+        strides = [tuple(x.stride()[:3]) for x in (q, k, v)]
+        lse_shape = (b, heads, sq)
+    if not _lse_ok(lse, lse_shape, dev):
         return None
-    if causal is not True and causal is not False:
-        return None
-    out = torch.empty((b, sq, heads, hd), dtype=q.dtype, device=dev)
-    if b == 0:
+    out = torch.empty(q.shape, dtype=q.dtype, device=dev)
+    if b == 0 or q.numel() == 0:
         return out
     stream = K.current_stream(dev)
-    arr = (K.i64x3(q.stride()[:3]), K.i64x3(k.stride()[:3]), K.i64x3(v.stride()[:3]))
+    arr = [K.i64x3(x) for x in strides]
     ws = K.workspace(dev, stream)
     with K.on_device(dev):
-        rc = K.library().ca_flash(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), b, sq, sk, heads, hd,
-                                  *arr, _scale(scale), int(causal), dt, ws.data_ptr(), stream)
+        rc = K.library().ca_flash_ex(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), lse.data_ptr() if lse is not None else None,
+            b, sq, sk, heads, kvh, hd, *arr, cu_q.data_ptr() if var else None, cu_k.data_ptr() if var else None,
+            tq, tk, _scale(scale), int(causal), dt, ws.data_ptr(), stream)
     if not _check_rc(rc):
         return None
+    if K.CHECK:
+        K.raise_status(dev, stream)
     return out

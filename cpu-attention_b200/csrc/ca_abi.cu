@@ -9,7 +9,7 @@
 #include <mutex>
 #include <string>
 
-#include "decode.cuh"
+#include "decode_launch.cuh"
 #include "flash.cuh"
 #include "flash_tc.cuh"
 #include "store.cuh"
@@ -58,53 +58,48 @@ int current_device(int* dev) {
 
 // ---- decode plan ---------------------------------------------------------
 struct DecodePlan {
-  int stages, warps, stage_bytes, kslot_bytes, page_bytes, warp_bytes, smem_bytes, ctas, pages_per_warp, task_cap, ahead, tail_div;
+  int gr;  // query rows per item (1, 2, 4, 8)
+  int stages, warps, stage_bytes, kslot_bytes, page_bytes, warp_bytes, smem_bytes, ctas, pages_per_warp, task_cap,
+      ahead, tail_div;
 };
 
 constexpr int kDecodeRingTarget = 16384;  // bytes of ring per warp
-constexpr int kTasksPerSm = 32;           // split tasks per SM at most (task_cap / SMs)
+constexpr int kTasksPerSm = 32;           // split tasks per SM at most (task_cap / SMs, one row per item)
 
-// Shared memory of the CTA-wide area behind the streaming warps' rings: the
-// task queue with its query rows, and the merge buffers.
-int decode_cta_extra(long long head_dim, int warps) { return ca::decode_cta_bytes((int)head_dim, warps); }
+// Query rows per decode item for `group` query heads per KV head: the group
+// rounded up to 1, 2, 4 or 8 (larger groups take several items).
+int decode_rows(long long group) {
+  if (group <= 1) return 1;
+  if (group == 2) return 2;
+  if (group <= 4) return 4;
+  return 8;
+}
 
-bool decode_plan(long long head_dim, long long page, int dtype, const DeviceInfo& dev, DecodePlan* pl) {
-  if (page > ca::kDecodeMaxPage) return false;
-  const long long page_bytes = page * head_dim * (long long)elem_size(dtype);
-  pl->page_bytes = (int)page_bytes;
-  pl->kslot_bytes = (int)page_bytes + ca::kKSlotPadBytes;
-  pl->stage_bytes = pl->kslot_bytes + (int)page_bytes;
-  const int budget = dev.max_smem_optin - 1024;
-  int stages = std::max(2, std::min(4, kDecodeRingTarget / pl->stage_bytes));
-  auto warp_bytes = [&](int s) { return ca::decode_warp_bytes(s, pl->stage_bytes); };
-  auto fits = [&](int s, int warps) { return warps * warp_bytes(s) + decode_cta_extra(head_dim, warps) <= budget; };
-  while (stages > 2 && !fits(stages, 1)) --stages;
-  if (!fits(stages, 1)) return false;
-  int warps = ca::kDecodeMaxWarps;
-  while (warps > 1 && !fits(stages, warps)) --warps;
-  pl->stages = stages;
-  pl->warps = warps;
-  pl->warp_bytes = warp_bytes(stages);
-  pl->smem_bytes = warps * pl->warp_bytes + decode_cta_extra(head_dim, warps);
-  pl->ctas = dev.sms;
-  // task unit: 5 pages per streaming warp (measured 1.5% faster than 4 on the
-  // ragged cfg2 workload, equal on the others)
-  pl->pages_per_warp = 5;
-  pl->task_cap = kTasksPerSm * dev.sms;
-  pl->ahead = ca::kDecodeAhead;
-  // the last tasks are half the size of the others (a third: +3% and -1% on
-  // cfg2 in two sweeps, -1.5% on the E=32 cross-attention case)
-  pl->tail_div = 2;
-  return true;
+int decode_cta_bytes(int gr, long long head_dim) {
+  switch (gr) {
+    case 1: return ca::DecodeCta<1>::bytes((int)head_dim);
+    case 2: return ca::DecodeCta<2>::bytes((int)head_dim);
+    case 4: return ca::DecodeCta<4>::bytes((int)head_dim);
+    default: return ca::DecodeCta<8>::bytes((int)head_dim);
+  }
+}
+int decode_warp_bytes(int gr, int stages, int stage_bytes) {
+  switch (gr) {
+    case 1: return ca::decode_warp_bytes<1>(stages, stage_bytes);
+    case 2: return ca::decode_warp_bytes<2>(stages, stage_bytes);
+    case 4: return ca::decode_warp_bytes<4>(stages, stage_bytes);
+    default: return ca::decode_warp_bytes<8>(stages, stage_bytes);
+  }
 }
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-// workspace: [status int32, task counter int32 | pad to 256][partials: float,
-// 2 * task_cap + 2 slots of (E + 2), fixed per device][tickets: int32 per
-// (sequence, head)]. The tickets sit at a fixed offset so that no call's
-// partials ever land on another call's tickets; the counter and the tickets
-// are zero between calls (the kernel leaves them so).
+// workspace: [status int32, task counter int32, the last launch's ticket count
+// and offset | pad to 256][partials: float, (2 * kTasksPerSm * SMs + 2) *
+// (128 + 2), fixed per device][tickets: int32 per (sequence, head)]. The
+// tickets sit at a fixed offset so that no call's partials ever land on
+// another call's tickets; the counter and the tickets are zero between calls
+// (the kernel leaves them so; ca_status clears them after a timeout).
 size_t decode_partial_bytes(const DeviceInfo& dev) {
   return align256((size_t)(2 * (size_t)kTasksPerSm * dev.sms + 2) * (128 + 2) * 4);
 }
@@ -112,31 +107,39 @@ size_t decode_ws_bytes(long long batch, long long heads, const DeviceInfo& dev) 
   return 256 + decode_partial_bytes(dev) + align256((size_t)(batch * heads) * 4);
 }
 
-template <typename T, int E>
-int launch_decode(const ca::DecodeParams& prm, const DecodePlan& pl, cudaStream_t stream, int device) {
-  static std::mutex mu;
-  static int configured[64] = {0};
-  auto kern = ca::decode_kernel<T, E>;
-  {
-    std::lock_guard<std::mutex> lock(mu);
-    if (configured[device] < pl.smem_bytes) {
-      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem_bytes);
-      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(decode)");
-      configured[device] = pl.smem_bytes;
-    }
-  }
-  kern<<<pl.ctas, 32 * (pl.warps + 2 + ca::kDecodeFinishers), pl.smem_bytes, stream>>>(prm);  // one persistent CTA per SM
-  cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? CA_OK : cuda_fail(e, "decode launch");
-}
-
-template <typename T>
-int dispatch_decode(long long E, const ca::DecodeParams& prm, const DecodePlan& pl, cudaStream_t s, int dev) {
-  switch (E) {
-    case 32: return launch_decode<T, 32>(prm, pl, s, dev);
-    case 64: return launch_decode<T, 64>(prm, pl, s, dev);
-    default: return launch_decode<T, 128>(prm, pl, s, dev);
-  }
+bool decode_plan(long long head_dim, long long page, int dtype, int gr, const DeviceInfo& dev, DecodePlan* pl) {
+  if (page > ca::kDecodeMaxPage) return false;
+  pl->gr = gr;
+  const long long page_bytes = page * head_dim * (long long)elem_size(dtype);
+  pl->page_bytes = (int)page_bytes;
+  pl->kslot_bytes = (int)page_bytes + ca::kKSlotPadBytes;
+  pl->stage_bytes = pl->kslot_bytes + (int)page_bytes;
+  const int budget = dev.max_smem_optin - 1024;
+  const int cta = decode_cta_bytes(gr, head_dim);
+  int stages = std::max(2, std::min(4, kDecodeRingTarget / pl->stage_bytes));
+  auto fits = [&](int s, int warps) { return warps * decode_warp_bytes(gr, s, pl->stage_bytes) + cta <= budget; };
+  while (stages > 2 && !fits(stages, 1)) --stages;
+  if (!fits(stages, 1)) return false;
+  int warps = ca::kDecodeMaxWarps;
+  while (warps > 1 && !fits(stages, warps)) --warps;
+  pl->stages = stages;
+  pl->warps = warps;
+  pl->warp_bytes = decode_warp_bytes(gr, stages, pl->stage_bytes);
+  pl->smem_bytes = warps * pl->warp_bytes + cta;
+  pl->ctas = dev.sms;
+  // task unit: 5 pages per streaming warp (measured 1.5% faster than 4 on the
+  // ragged cfg2 workload, equal on the others)
+  pl->pages_per_warp = 5;
+  // split tasks keep within the partial area: slots of gr rows of
+  // (head_dim + 2) floats, at most 2 * task_cap + 2 of them
+  const long long slots = (long long)(decode_partial_bytes(dev) / 4) / ((long long)gr * (head_dim + 2));
+  pl->task_cap = (int)std::min<long long>((long long)kTasksPerSm * dev.sms, (slots - 2) / 2);
+  if (pl->task_cap < dev.sms) return false;
+  pl->ahead = ca::kDecodeAhead;
+  // the last tasks are half the size of the others (a third: +3% and -1% on
+  // cfg2 in two sweeps, -1.5% on the E=32 cross-attention case)
+  pl->tail_div = 2;
+  return true;
 }
 
 template <typename T, int E>
@@ -207,7 +210,7 @@ size_t ca_decode_workspace_bytes(int64_t batch, int64_t heads, int64_t head_dim,
   DeviceInfo dev;
   if (device_info(device, &dev) != CA_OK) return 0;
   DecodePlan pl;
-  if (!head_dim_ok(head_dim) || !page_ok(page) || !decode_plan(head_dim, page, dtype, dev, &pl)) return 0;
+  if (!head_dim_ok(head_dim) || !page_ok(page) || !decode_plan(head_dim, page, dtype, 1, dev, &pl)) return 0;
   return decode_ws_bytes(batch, heads, dev);
 }
 
@@ -215,37 +218,42 @@ size_t ca_decode_workspace_bytes(int64_t batch, int64_t heads, int64_t head_dim,
 
 namespace {
 
-// ca_decode and ca_decode_append: n_new tokens per sequence (k_new rows
-// kv_stride apart between sequences, kv_tstride between tokens), stored by
-// slot (n_new == 1 only) or appended at lens[i].
+// Every decode entry: n_new tokens per sequence (k_new rows kv_stride apart
+// between sequences, kv_tstride between tokens), stored by slot (n_new == 1
+// only) or appended at lens[i]; kv_heads KV heads shared by groups of
+// heads / kv_heads query heads; the rows' log-sum-exp into lse when given.
 int decode_impl(const void* q, int64_t q_stride, void* k_cache, void* v_cache, int64_t num_blocks,
                 const void* k_new, const void* v_new, int64_t kv_stride, int64_t kv_tstride, int64_t n_new,
                 const int64_t* slots, const int32_t* lens, const int32_t* page_table, int64_t table_width,
-                void* out, int64_t batch, int64_t heads, int64_t head_dim, int64_t page, int dtype,
-                float softmax_scale, void* workspace, size_t workspace_bytes, void* stream) {
+                void* out, float* lse, int64_t batch, int64_t heads, int64_t kv_heads, int64_t head_dim,
+                int64_t page, int dtype, float softmax_scale, void* workspace, size_t workspace_bytes,
+                void* stream) {
   if (dtype != CA_DTYPE_F32 && dtype != CA_DTYPE_BF16) return CA_EDTYPE;
   if (!head_dim_ok(head_dim)) return CA_EHEADDIM;
   if (!page_ok(page)) return CA_EPAGE;
-  if (batch < 0 || heads <= 0 || num_blocks < 0 || table_width < 0) return CA_ESHAPE;
+  if (batch < 0 || heads <= 0 || kv_heads <= 0 || num_blocks < 0 || table_width < 0) return CA_ESHAPE;
+  if (heads % kv_heads || heads > (1 << 16) || batch > (1 << 24) || batch * heads > (1LL << 30)) return CA_ESHAPE;
   if ((k_new == nullptr) != (v_new == nullptr)) return CA_ESHAPE;
   if (slots && !k_new) return CA_ESHAPE;  // `_C.mojo:140-143`
   if (batch == 0) return CA_OK;
   if (!q || !k_cache || !v_cache || !lens || !page_table || !out || !workspace) return CA_ENULL;
   if (q_stride < heads * head_dim) return CA_ELAYOUT;
-  if (k_new && kv_stride < heads * head_dim) return CA_ELAYOUT;
-  if (k_new && n_new > 1 && (kv_tstride < heads * head_dim || kv_stride < n_new * kv_tstride)) return CA_ELAYOUT;
+  if (k_new && kv_stride < kv_heads * head_dim) return CA_ELAYOUT;
+  if (k_new && n_new > 1 && (kv_tstride < kv_heads * head_dim || kv_stride < n_new * kv_tstride))
+    return CA_ELAYOUT;
   if (n_new < 0 || n_new > (1 << 20) || (slots && n_new != 1)) return CA_ESHAPE;
   // whole pages move by 16-byte bulk copies
   if (!aligned(k_cache, 16) || !aligned(v_cache, 16)) return CA_ELAYOUT;
   const size_t es = elem_size(dtype);
-  if (!aligned(q, es) || !aligned(out, es)) return CA_ELAYOUT;
+  if (!aligned(q, es) || !aligned(out, es) || !aligned(lse, 4)) return CA_ELAYOUT;
   int device;
   int rc = current_device(&device);
   if (rc) return rc;
   DeviceInfo dev;
   if ((rc = device_info(device, &dev))) return rc;
+  const long long group = heads / kv_heads;
   DecodePlan pl;
-  if (!decode_plan(head_dim, page, dtype, dev, &pl)) return CA_EUNSUPPORTED;
+  if (!decode_plan(head_dim, page, dtype, decode_rows(group), dev, &pl)) return CA_EUNSUPPORTED;
   if (workspace_bytes < decode_ws_bytes(batch, heads, dev)) return CA_EWORKSPACE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   char* ws = static_cast<char*>(workspace);
@@ -271,7 +279,7 @@ int decode_impl(const void* q, int64_t q_stride, void* k_cache, void* v_cache, i
     sp.page_table = page_table;
     sp.pt_stride = table_width;
     sp.tokens = batch;
-    sp.H = (int)heads;
+    sp.H = (int)kv_heads;
     sp.page = (int)page;
     sp.status = status;
     const bool vec16 = aligned(k_new, 16) && aligned(v_new, 16) && (kv_stride * es) % 16 == 0;
@@ -295,8 +303,13 @@ int decode_impl(const void* q, int64_t q_stride, void* k_cache, void* v_cache, i
   prm.pt_stride = table_width;
   prm.out = out;
   prm.out_stride = heads * head_dim;
+  prm.lse = lse;
   prm.B = (int)batch;
   prm.H = (int)heads;
+  prm.Hk = (int)kv_heads;
+  prm.G = (int)group;
+  prm.NRG = (int)((group + pl.gr - 1) / pl.gr);
+  prm.IH = prm.Hk * prm.NRG;
   prm.page = (int)page;
   const double scale = std::isnan(softmax_scale) ? 1.0 / std::sqrt((double)head_dim) : (double)softmax_scale;
   prm.c = (float)(scale * 1.4426950408889634);
@@ -315,8 +328,14 @@ int decode_impl(const void* q, int64_t q_stride, void* k_cache, void* v_cache, i
   prm.status = status;
   const uint64_t wl = g_wait_ns.load();
   prm.wait_ns = wl ? wl : ca::kWaitLimitNs;
-  if (dtype == CA_DTYPE_BF16) return dispatch_decode<__nv_bfloat16>(head_dim, prm, pl, s, device);
-  return dispatch_decode<float>(head_dim, prm, pl, s, device);
+  const int threads = 32 * (pl.warps + 2 + ca::kDecodeFinishers);
+  const char* what = "decode";
+  const cudaError_t e =
+      dtype == CA_DTYPE_BF16
+          ? ca::decode_dispatch<__nv_bfloat16>((int)head_dim, pl.gr, prm, pl.ctas, threads, pl.smem_bytes, s,
+                                               device, &what)
+          : ca::decode_dispatch<float>((int)head_dim, pl.gr, prm, pl.ctas, threads, pl.smem_bytes, s, device, &what);
+  return e == cudaSuccess ? CA_OK : cuda_fail(e, what);
 }
 
 }  // namespace
@@ -329,8 +348,8 @@ int ca_decode(const void* q, int64_t q_stride, void* k_cache, void* v_cache, int
               int64_t head_dim, int64_t page, int dtype, float softmax_scale, void* workspace,
               size_t workspace_bytes, void* stream) {
   return decode_impl(q, q_stride, k_cache, v_cache, num_blocks, k_new, v_new, kv_stride, 0, k_new ? 1 : 0, slots,
-                     lens, page_table, table_width, out, batch, heads, head_dim, page, dtype, softmax_scale,
-                     workspace, workspace_bytes, stream);
+                     lens, page_table, table_width, out, nullptr, batch, heads, heads, head_dim, page, dtype,
+                     softmax_scale, workspace, workspace_bytes, stream);
 }
 
 int ca_decode_append(const void* q, int64_t q_stride, void* k_cache, void* v_cache, int64_t num_blocks,
@@ -340,36 +359,62 @@ int ca_decode_append(const void* q, int64_t q_stride, void* k_cache, void* v_cac
                      void* workspace, size_t workspace_bytes, void* stream) {
   if (n_new < 1 || !k_new || !v_new) return CA_ESHAPE;
   return decode_impl(q, q_stride, k_cache, v_cache, num_blocks, k_new, v_new, kv_stride, kv_token_stride, n_new,
-                     nullptr, lens, page_table, table_width, out, batch, heads, head_dim, page, dtype,
+                     nullptr, lens, page_table, table_width, out, nullptr, batch, heads, heads, head_dim, page, dtype,
                      softmax_scale, workspace, workspace_bytes, stream);
 }
 
-int ca_flash(const void* q, const void* k, const void* v, void* out, int64_t batch, int64_t seq_q, int64_t seq_k,
-             int64_t heads, int64_t head_dim, const int64_t q_strides[3], const int64_t k_strides[3],
-             const int64_t v_strides[3], float softmax_scale, int causal, int dtype, int32_t* status,
-             void* stream) {
+int ca_decode_ex(const void* q, int64_t q_stride, void* k_cache, void* v_cache, int64_t num_blocks,
+                 const void* k_new, const void* v_new, int64_t kv_stride, int64_t kv_token_stride, int64_t n_new,
+                 const int64_t* slots, const int32_t* lens, const int32_t* page_table, int64_t table_width,
+                 void* out, float* lse, int64_t batch, int64_t heads, int64_t kv_heads, int64_t head_dim,
+                 int64_t page, int dtype, float softmax_scale, void* workspace, size_t workspace_bytes,
+                 void* stream) {
+  if ((k_new == nullptr) != (n_new == 0)) return CA_ESHAPE;
+  return decode_impl(q, q_stride, k_cache, v_cache, num_blocks, k_new, v_new, kv_stride, kv_token_stride, n_new,
+                     slots, lens, page_table, table_width, out, lse, batch, heads, kv_heads, head_dim, page, dtype,
+                     softmax_scale, workspace, workspace_bytes, stream);
+}
+
+int ca_flash_ex(const void* q, const void* k, const void* v, void* out, float* lse, int64_t batch, int64_t seq_q,
+                int64_t seq_k, int64_t heads, int64_t kv_heads, int64_t head_dim, const int64_t q_strides[3],
+                const int64_t k_strides[3], const int64_t v_strides[3], const int32_t* cu_seqlens_q,
+                const int32_t* cu_seqlens_k, int64_t total_q, int64_t total_k, float softmax_scale, int causal,
+                int dtype, int32_t* status, void* stream) {
   if (dtype != CA_DTYPE_F32 && dtype != CA_DTYPE_BF16) return CA_EDTYPE;
   if (!head_dim_ok(head_dim)) return CA_EHEADDIM;
-  if (batch < 0 || seq_q < 1 || seq_k < 1 || heads <= 0) return CA_ESHAPE;
-  if (batch == 0) return CA_OK;
+  const bool var = cu_seqlens_q != nullptr || cu_seqlens_k != nullptr;
+  if (batch < 0 || seq_q < 1 || seq_k < 1 || heads <= 0 || kv_heads <= 0 || heads % kv_heads) return CA_ESHAPE;
+  if (seq_q > 0x7fffffffLL || seq_k > 0x7fffffffLL || heads > 0xffffLL || batch > 0x7fffffffLL) return CA_ESHAPE;
+  if (var && (!cu_seqlens_q || !cu_seqlens_k || total_q < 0 || total_k < 0 || total_q > 0x7fffffffLL ||
+              total_k > 0x7fffffffLL))
+    return CA_ESHAPE;
+  if (batch == 0 || (var && total_q == 0)) return CA_OK;
   if (!q || !k || !v || !out || !q_strides || !k_strides || !v_strides) return CA_ENULL;
   const size_t es = elem_size(dtype);
-  if (!aligned(q, es) || !aligned(k, es) || !aligned(v, es) || !aligned(out, es)) return CA_ELAYOUT;
+  if (!aligned(q, es) || !aligned(k, es) || !aligned(v, es) || !aligned(out, es) || !aligned(lse, 4))
+    return CA_ELAYOUT;
   const double scale = std::isnan(softmax_scale) ? 1.0 / std::sqrt((double)head_dim) : (double)softmax_scale;
   ca::FlashParams prm{};
   prm.q = q;
   prm.k = k;
   prm.v = v;
   prm.out = out;
+  prm.lse = lse;
   prm.B = (int)batch;
   prm.Lq = (int)seq_q;
   prm.Lk = (int)seq_k;
   prm.H = (int)heads;
+  prm.Hk = (int)kv_heads;
+  prm.G = (int)(heads / kv_heads);
   for (int i = 0; i < 3; ++i) {
     prm.qs[i] = q_strides[i];
     prm.ks[i] = k_strides[i];
     prm.vs[i] = v_strides[i];
   }
+  prm.cu_q = cu_seqlens_q;
+  prm.cu_k = cu_seqlens_k;
+  prm.total_q = var ? total_q : 0;
+  prm.total_k = var ? total_k : 0;
   prm.c = (float)(scale * 1.4426950408889634);
   prm.causal = causal ? 1 : 0;
   int device;
@@ -378,6 +423,14 @@ int ca_flash(const void* q, const void* k, const void* v, void* out, int64_t bat
   DeviceInfo dev;
   if ((rc = device_info(device, &dev))) return rc;
   return ca::flash_launch(prm, (int)head_dim, dtype, status, static_cast<cudaStream_t>(stream), &g_cuda_error);
+}
+
+int ca_flash(const void* q, const void* k, const void* v, void* out, int64_t batch, int64_t seq_q, int64_t seq_k,
+             int64_t heads, int64_t head_dim, const int64_t q_strides[3], const int64_t k_strides[3],
+             const int64_t v_strides[3], float softmax_scale, int causal, int dtype, int32_t* status,
+             void* stream) {
+  return ca_flash_ex(q, k, v, out, nullptr, batch, seq_q, seq_k, heads, heads, head_dim, q_strides, k_strides,
+                     v_strides, nullptr, nullptr, 0, 0, softmax_scale, causal, dtype, status, stream);
 }
 
 int ca_status(void* workspace, int reset, void* stream) {

@@ -1,50 +1,58 @@
 // Paged one-token decode (flash_attn_with_kvcache) for sm_100a.
 //
 // What it computes restates `paged_attn.mojo:714-782` (`_attend`): for every
-// (sequence i, head h), one query row q[i,h,:] against the first L_i cached
-// tokens of its pages (L_i = cache_seqlens[i] + 1 when the call appended a
-// token through the page table, `paged_attn.mojo:723-725`):
+// (sequence i, query head h), one query row q[i,h,:] against the first L_i
+// cached tokens of its KV head's pages (L_i = cache_seqlens[i] + 1 when the
+// call appended a token through the page table, `paged_attn.mojo:723-725`):
 //     x_t = (q . k_t) * scale * log2(e)          (fp32, exact bf16 products)
 //     m   = max_t x_t,  p_t = 2^(x_t - m),  l = sum_t p_t
 //     out = (sum_t p_t v_t) * (1 / l)           (0 when l == 0, `:297-310`)
+//     lse = (m + log2 l) * ln 2                 (optional; -inf when l == 0)
 // computed page by page in log2 units and combined with FlashAttention's
 // rescaling, always in page order, so the result does not depend on which
 // warp or SM streamed which page (it is bitwise reproducible).
 //
+// Grouped heads (GQA/MQA, kv_heads < heads; the reference declines them,
+// `flash_attn_interface.py:144-145`): the G = heads / kv_heads query heads of
+// a KV head read the same pages, so an item is (sequence, KV head, a group of
+// up to GR of its query heads) and every page staged in shared memory serves
+// all GR rows: a page crosses HBM once per item, and once per KV head when
+// G <= GR. GR (1, 2, 4 or 8) is a template parameter; MHA is GR = 1.
+//
 // How it runs on the B200 (nothing here is a translation of the CPU drivers):
 //   * Work is cut into tasks: a task is a run of consecutive pages of one
-//     item (sequence i, head h), the item's pages split evenly into
-//     ceil(np / U) tasks, numbered in (sequence, head, piece) order. U is
-//     five pages per streaming warp by default (more when the workload is
-//     huge; the host sets it); the
-//     sequences holding the last eighth of the pages use U / 2, so the tasks
-//     handed out last are short and the SMs run out of work together.
+//     item, the item's pages split evenly into ceil(np / U) tasks, numbered in
+//     (sequence, item, piece) order. U is five pages per streaming warp by
+//     default (more when the workload is huge); the sequences holding the last
+//     eighth of the pages use U / 2, so the tasks handed out last are short
+//     and the SMs run out of work together.
 //   * A persistent grid of one CTA per SM: CTA c starts on task c, then takes
 //     tasks from an atomic counter, so SMs that stream slower take fewer (the
 //     last failing grab resets the counter for the next call).
 //   * Inside a CTA, warp roles: W streaming warps, a feeder, a merger and two
 //     finishers, talking through shared memory only (bounded spins, no
 //     CTA-wide barrier):
-//       - the feeder keeps one task staged (grabbed, located, its query row
+//       - the feeder keeps one task staged (grabbed, located, its query rows
 //         and block ids loaded) and publishes it in a queue when the streaming
 //         warps are about to need it: an entry (item, pages, position in the
-//         CTA's page stream), the query row in fp32 and the block ids in a
+//         CTA's page stream), the query rows in fp32 and the block ids in a
 //         ring. Near the end of the pool it grabs only when needed.
 //       - streaming warps claim pages of the CTA's page stream one at a time
 //         (a shared counter), so every warp stays busy whatever the task
 //         sizes. A claimed page's K and V arrive by 1-D bulk copies
 //         (cp.async.bulk, the TMA engine; L2 evict-first) into the warp's own
 //         ring of stages, completing on one mbarrier per stage. The warp
-//         computes the page's (m, l, acc) and deposits it in the page's slot
-//         of a 24-slot ring.
+//         computes the page's (m, l, acc) of each row and deposits them in the
+//         page's slot of a ring.
 //       - the merger folds the page states of each task in page order, then
-//         writes the output row, or hands a split task's state on.
-//       - the finishers write a split task's partial (m, l, acc) to the
+//         writes the output rows, or hands a split task's states on.
+//       - the finishers write a split task's partials (m, l, acc) to the
 //         workspace and take the item's ticket; the item's last task merges
-//         all of its partials, in task order, into the output row.
+//         all of its partials, in task order, into the output rows.
 //   * Q.K^T: lane = key, reading the dim-pair-major K page with conflict-free
 //     32-bit shared loads (a 16-key page: half-warps split the K rows) against
-//     the fp32 query as broadcast loads; P.V: lanes own 4 dims of a V row.
+//     the fp32 query rows as broadcast loads, each K word feeding every row;
+//     P.V: lanes own 4 dims of a V row, each V word feeding every row.
 //   * Masked keys never reach P.V (the loop stops at the last valid key), so
 //     NaN in unused slots of a page cannot leak (`paged_attn.mojo:686-687`).
 //   * Start-up: the first copies wait for three dependent round trips (the
@@ -55,8 +63,8 @@
 //   * An append through the page table (one token, or several: a prompt) is
 //     fused: the warp that streams a page holding new tokens patches them
 //     into shared memory after the copy lands and writes them to the cache
-//     (it is that page's only reader in the call), so no second launch is
-//     needed.
+//     (the first item of the KV head writes; it is that page's only writer in
+//     the call), so no second launch is needed.
 #pragma once
 
 #include "common.cuh"
@@ -65,18 +73,24 @@ namespace ca {
 
 constexpr int kDecodeMaxPage = 128;               // tokens per page this kernel stages
 constexpr int kKSlotPadBytes = 64;                // K page slot padding: 16 banks
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s per bounded wait
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s per bounded wait (default)
 constexpr int kDecodeMaxWarps = 12;               // streaming warps per CTA (plus a merger, a feeder and the finishers)
-constexpr int kDecodeQueue = 8;                   // task queue entries per CTA
 constexpr int kDecodeAhead = 12;                  // published pages a CTA keeps unclaimed
-constexpr int kDecodeFinish = 4;                  // split tasks in flight from the merger to the finishers
 constexpr int kDecodeFinishers = 2;               // finisher warps (entry f goes to finisher f % 2)
-constexpr int kDecodePageSlots = 24;              // page states in flight to the merger
 constexpr int kDecodeBlkRing = 512;               // staged block ids per CTA (a ring over the page stream)
 constexpr int kDecodeBlkTask = 256;               // tasks up to this many pages stage their block ids
 constexpr int kSpinSleepNs = 32;                  // sleep between polls of a spinning warp
 constexpr int kDecodeWarmPages = 16;              // pages of its own item each CTA pulls into L2 at the start
 constexpr int kPlanRegs = 4;                      // plan: page counts of 32 sequences per register kept
+
+// Shared-memory rings whose entries hold GR query rows each, sized per GR so
+// that the streaming warps keep most of the shared memory.
+template <int GR>
+struct DecodeRings {
+  static constexpr int QD = GR <= 2 ? 8 : (GR == 4 ? 6 : 4);                     // task queue entries
+  static constexpr int R = GR == 1 ? 24 : (GR == 2 ? 16 : (GR == 4 ? 12 : 10));  // page states in flight
+  static constexpr int FQ = GR <= 4 ? 4 : 2;  // split tasks in flight from the merger to the finishers
+};
 
 struct DecodeParams {
   const void* q;
@@ -94,7 +108,12 @@ struct DecodeParams {
   long long pt_stride;  // table width W
   void* out;
   long long out_stride;  // elements between sequences
+  float* lse;            // [B, H] log-sum-exp of each row (natural log), or NULL
   int B, H, page;
+  int Hk;   // KV heads (the caches' heads)
+  int G;    // query heads per KV head (H / Hk)
+  int NRG;  // items per KV head: ceil(G / GR)
+  int IH;   // items per sequence: Hk * NRG
   float c;  // softmax_scale * log2(e)
   // plan (host)
   int stages;          // ring depth per warp
@@ -106,9 +125,9 @@ struct DecodeParams {
   int pages_per_warp;  // task size U = warps * pages_per_warp (or more)
   int ahead;           // published pages the feeder keeps unclaimed
   int tail_div;        // the last tasks are 1 / tail_div the size of the others
-  int task_cap;        // tasks of split items number at most 2 * task_cap
-  float* partial;      // [2 * task_cap + 2][E + 2]
-  int* tickets;        // [B * H], zero between calls
+  int task_cap;        // split tasks number at most 2 * task_cap
+  float* partial;      // [2 * task_cap + 2][GR][E + 2]
+  int* tickets;        // [B * IH], zero between calls
   int* status;         // CA_STATUS_* bits; status[2], status[3]: this call's ticket count and byte offset
   int* counter;        // tasks handed out, zero between calls
   unsigned long long wait_ns;  // limit of each bounded wait on another warp or a copy
@@ -148,7 +167,7 @@ struct TaskPlan {
 
 // Where a task lives.
 struct Task {
-  int i, h;        // item
+  int i, ih;       // item: sequence i, item ih of the sequence
   int np, len;     // pages and attended length of sequence i
   int raw;         // cache_seqlens[i] as given
   int ntask, j;    // tasks of the item, and which one this is
@@ -172,7 +191,7 @@ struct TaskWalk {
         np = seq_pages(p, i, &L);
         nt = item_tasks(np, plan.size(i));
       }
-      const int tk = nt * p.H, sl = nt > 1 ? tk : 0;
+      const int tk = nt * p.IH, sl = nt > 1 ? tk : 0;
       const int tincl = warp_scan_i(tk, lane) + tbase;
       const int sincl = warp_scan_i(sl, lane) + sbase;
       const unsigned hit = __ballot_sync(0xffffffffu, i < p.B && tincl > tid);
@@ -186,8 +205,8 @@ struct TaskWalk {
         const int t0 = __shfl_sync(0xffffffffu, tincl - tk, src);
         const int s0 = __shfl_sync(0xffffffffu, sincl - sl, src);
         const int off = tid - t0;
-        t.h = off / t.ntask;
-        t.j = off - t.h * t.ntask;
+        t.ih = off / t.ntask;
+        t.j = off - t.ih * t.ntask;
         t.pg0 = (int)div_pos((long long)t.j * t.np, t.ntask);  // even split of the item's pages
         t.pg1 = (int)div_pos((long long)(t.j + 1) * t.np, t.ntask);
         t.slot = t.ntask > 1 ? s0 + off : -1;
@@ -225,7 +244,11 @@ __device__ __forceinline__ bool decode_wait(uint64_t* bar, uint32_t parity, vola
 // the streaming warps and the merger until the merger is done with it).
 struct QueueEntry {
   int id;          // task id, -1: no more tasks
-  int i, h;        // item
+  int i;           // sequence
+  int hk;          // KV head
+  int h0, nrows;   // query heads [h0, h0 + nrows) of the item
+  int item;        // the item's ticket index: i * IH + ih
+  int gw;          // 1: this item writes the appended tokens to the cache
   int ntask, j;    // tasks of the item, and which one this is
   int pg0;         // first page of the task
   int n;           // pages of the task
@@ -238,27 +261,34 @@ struct QueueEntry {
 };
 
 // A split task's merged state on its way from the merger to the finisher.
+template <int GR>
 struct FinishEntry {
-  int i, h, ntask, j;  // i < 0: no more
+  int i, h0, nrows, item, ntask, j;  // i < 0: no more
   long long slot;
-  float m, l;
+  float m[GR], l[GR];
 };
 
 // CTA area after the streaming warps' rings (byte offsets; the host sizes it
-// with decode_cta_bytes).
-constexpr int kCtaInts = 0;                       // counters and flags, see the kernel
-constexpr int kCtaEntries = 4 * 128;              // QueueEntry[kDecodeQueue]
-constexpr int kCtaFinish = kCtaEntries + (int)sizeof(QueueEntry) * kDecodeQueue;  // FinishEntry[kDecodeFinish]
-constexpr int kCtaRows = kCtaFinish + (int)sizeof(FinishEntry) * kDecodeFinish;   // float rows
-__host__ __device__ constexpr int decode_cta_bytes(int E, int warps) {
-  // query rows [QD][E], finisher accumulators [FQ][E], page states [R][E + 4], block ids [RB]
-  return kCtaRows + kDecodeQueue * E * 4 + kDecodeFinish * E * 4 + kDecodePageSlots * (E + 4) * 4 +
-         kDecodeBlkRing * 4 + 0 * warps;
-}
-// Per streaming warp, behind its ring: probabilities, stage tags (task
-// position, page, stream index; 16-byte aligned), stage barriers.
+// with DecodeCta<GR>::bytes).
+template <int GR>
+struct DecodeCta {
+  using Rg = DecodeRings<GR>;
+  static constexpr int kInts = 0;  // counters and flags, see the kernel
+  static constexpr int kEntries = 4 * 128;
+  static constexpr int kFinish = kEntries + (int)sizeof(QueueEntry) * Rg::QD;
+  static constexpr int kRows = (kFinish + (int)sizeof(FinishEntry<GR>) * Rg::FQ + 15) / 16 * 16;
+  // query rows [QD][GR][E], finisher accumulators [FQ][GR][E], page states
+  // [R][GR][E + 4], block ids [RB]
+  static __host__ __device__ constexpr int bytes(int E) {
+    return kRows + Rg::QD * GR * E * 4 + Rg::FQ * GR * E * 4 + Rg::R * GR * (E + 4) * 4 + kDecodeBlkRing * 4;
+  }
+};
+
+// Per streaming warp, behind its ring: probabilities of GR rows, stage tags
+// (task position, page, stream index; 16-byte aligned), stage barriers.
+template <int GR>
 __host__ __device__ constexpr int decode_warp_bytes(int stages, int stage_bytes) {
-  return (stages * stage_bytes + kDecodeMaxPage * 4 + stages * 8 + stages * 16 + 127) / 128 * 128;
+  return (stages * stage_bytes + GR * kDecodeMaxPage * 4 + stages * 8 + stages * 16 + 127) / 128 * 128;
 }
 
 // Spins until `ok()` (bounded by `limit` ns; false on timeout or abort).
@@ -273,18 +303,27 @@ __device__ __forceinline__ bool spin_until(F ok, volatile int* abort, uint64_t l
   }
 }
 
-template <typename T, int E>
+// log-sum-exp in natural-log units of a row whose merged state is (m, l) in
+// log2 units
+__device__ __forceinline__ float row_lse(float m, float l) {
+  return l > 0.f ? (m + log2f(l)) * 0.69314718055994531f : -INFINITY;
+}
+
+template <typename T, int E, int GR>
 __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers), 1) decode_kernel(const __grid_constant__ DecodeParams p) {
   using Tile = DecodeTile<T, E>;
+  using Cta = DecodeCta<GR>;
+  using FinE = FinishEntry<GR>;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   const int lane = threadIdx.x & 31;
   const int w = threadIdx.x >> 5;
   const int W = p.warps;  // streaming warps; then the merger, the feeder and the finishers
-  constexpr int QD = kDecodeQueue, FQ = kDecodeFinish, R = kDecodePageSlots;
+  constexpr int QD = DecodeRings<GR>::QD, FQ = DecodeRings<GR>::FQ, R = DecodeRings<GR>::R;
+  constexpr int RS = E + 4;  // floats of one row's page state: acc[E], m, l (padded)
 
   // ---- CTA area
   uint8_t* cta = smem_raw + (size_t)W * p.warp_bytes;
-  volatile int* sInts = reinterpret_cast<volatile int*>(cta + kCtaInts);
+  volatile int* sInts = reinterpret_cast<volatile int*>(cta + Cta::kInts);
   volatile int* sSeq = sInts;                  // [QD] queue entry r holds task position sSeq[r] (-1: being written)
   volatile int* sFlag = sInts + QD;            // [R] page slot r holds stream page sFlag[r]
   volatile int* sFin = sInts + QD + R;         // [FQ] finisher entry r holds split task sFin[r]
@@ -293,16 +332,16 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
   volatile int* sAbort = sFin + FQ + 2;
   int* sNext = const_cast<int*>(sFin + FQ + 3);  // stream pages claimed
   volatile int* sFinAck = sFin + FQ + 4;       // [FQ] finisher entry r was last taken for split task sFinAck[r]
-  volatile QueueEntry* sQe = reinterpret_cast<volatile QueueEntry*>(cta + kCtaEntries);
-  volatile FinishEntry* sFe = reinterpret_cast<volatile FinishEntry*>(cta + kCtaFinish);
-  float* sRows = reinterpret_cast<float*>(cta + kCtaRows);  // [QD][E]
-  float* sFinO = sRows + QD * E;                              // [FQ][E]
-  float* sPage = sFinO + FQ * E;                              // [R][E + 4]: acc[E], m, l
-  int* sBlk = reinterpret_cast<int*>(sPage + R * (E + 4));   // [RB]: block id of stream page g at g % RB
+  volatile QueueEntry* sQe = reinterpret_cast<volatile QueueEntry*>(cta + Cta::kEntries);
+  volatile FinE* sFe = reinterpret_cast<volatile FinE*>(cta + Cta::kFinish);
+  float* sRows = reinterpret_cast<float*>(cta + Cta::kRows);  // [QD][GR][E]
+  float* sFinO = sRows + QD * GR * E;                         // [FQ][GR][E]
+  float* sPage = sFinO + FQ * GR * E;                         // [R][GR][RS]: acc[E], m, l
+  int* sBlk = reinterpret_cast<int*>(sPage + R * GR * RS);   // [RB]: block id of stream page g at g % RB
 
   uint8_t* wbase = smem_raw + (size_t)w * p.warp_bytes;
-  float* sP = reinterpret_cast<float*>(wbase + (size_t)p.stages * p.stage_bytes);
-  int4* sTag = reinterpret_cast<int4*>(sP + kDecodeMaxPage);  // per stage: task position, page, stream page
+  float* sP = reinterpret_cast<float*>(wbase + (size_t)p.stages * p.stage_bytes);  // [GR][kDecodeMaxPage]
+  int4* sTag = reinterpret_cast<int4*>(sP + GR * kDecodeMaxPage);  // per stage: task position, page, stream page
   uint64_t* sBar = reinterpret_cast<uint64_t*>(sTag + p.stages);
   if (threadIdx.x < 128)
     sInts[threadIdx.x] = (threadIdx.x < QD + R + FQ || (threadIdx.x >= QD + R + FQ + 4 && threadIdx.x < QD + R + 2 * FQ + 4)) ? -1 : 0;
@@ -318,7 +357,7 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
     // ================================================================= feeder
     // the call's ticket range, for the host to clear after a timeout (ca_status)
     if (blockIdx.x == 0 && lane == 0) {
-      p.status[2] = p.B * p.H;
+      p.status[2] = p.B * p.IH;
       p.status[3] = (int)(reinterpret_cast<char*>(p.tickets) - reinterpret_cast<char*>(p.status));
     }
     // ---- plan: task sizes and the number of tasks (only the feeder needs
@@ -327,7 +366,7 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
     // the later passes.
     constexpr int PR = kPlanRegs;
     int npr[PR];
-    int NP1 = 0, NT1 = 0;  // per head: pages, tasks (the totals are H times these)
+    int NP1 = 0, NT1 = 0;  // per item: pages, tasks (the totals are IH times these)
     for (int i0 = 0, k = 0; i0 < p.B; i0 += 32, ++k) {
       const int i = i0 + lane;
       int L, np = 0;
@@ -348,8 +387,8 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
       }
       return np;
     };
-    const int NPh = warp_sum_i(NP1);  // pages per head (every head of a sequence has the same)
-    const long long NP = (long long)NPh * p.H;
+    const int NPh = warp_sum_i(NP1);  // pages per item (every item of a sequence has the same)
+    const long long NP = (long long)NPh * p.IH;
     TaskPlan plan;
     plan.Ub = W * p.pages_per_warp;
     if (NP > (long long)p.task_cap * plan.Ub) plan.Ub = (int)div_pos(NP + p.task_cap - 1, p.task_cap);
@@ -357,7 +396,7 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
     plan.icut = p.B;
     if (plan.Us < plan.Ub) {
       // the first sequence from which on at most an eighth of the pages remain
-      // (in pages per head)
+      // (in pages per item)
       const int need = NPh - NPh / 8;
       int base = 0;
       for (int i0 = 0, k = 0; i0 < p.B && plan.icut == p.B; i0 += 32, ++k) {
@@ -373,7 +412,7 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
           base = __shfl_sync(0xffffffffu, before + pg, 31);
         }
       }
-      const long long tail = NP - (long long)base * p.H;  // pages of the small tasks
+      const long long tail = NP - (long long)base * p.IH;  // pages of the small tasks
       // only when every CTA gets a small task or more, and the split tasks keep
       // within the partial slots (at most 2 np / U slots per split item)
       if (plan.icut == p.B || tail < (long long)gridDim.x * plan.Us ||
@@ -385,9 +424,9 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
       const int np = pages_of(i0, k);
       if (i < p.B) NT1 += item_tasks(np, plan.size(i));
     }
-    const int NT = warp_sum_i(NT1) * p.H;
+    const int NT = warp_sum_i(NT1) * p.IH;
 
-    // Keeps one task staged (grabbed, located, its query row in registers)
+    // Keeps one task staged (grabbed, located, its query rows in registers)
     // and publishes it while fewer than p.ahead published pages are unclaimed
     // and a queue entry is free (merged); then stages the next, so the grab's
     // and the loads' latency overlap the wait. Every CTA makes exactly one
@@ -397,8 +436,9 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
     constexpr int QR = (E + 31) / 32;
     constexpr int BR = kDecodeBlkTask / 32;
     int sid = -1, sapg0 = 0, sapg1 = -1;  // staged task id (-1: the failing grab), its appended pages
+    int shk = 0, sh0 = 0, snr = 0;        // its KV head, first query head and rows
     Task st;
-    T qraw[QR];
+    T qraw[GR][QR];
     int sblk[BR];  // the task's block ids (tasks of at most kDecodeBlkTask pages)
     // Task c < gridDim.x is CTA c's first task; the others come from the
     // counter (id = gridDim.x + counter). Each CTA with a first task makes
@@ -420,10 +460,16 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
       sid = id;
       if (sid < 0) return;
       st = walk.locate(p, plan, sid, lane);
-      const T* qr = qbase + (long long)st.i * p.q_stride + (long long)st.h * E;
+      shk = st.ih / p.NRG;
+      const int rg = st.ih - shk * p.NRG;
+      sh0 = shk * p.G + rg * GR;
+      snr = min(GR, p.G - rg * GR);
+      const T* qr = qbase + (long long)st.i * p.q_stride + (long long)sh0 * E;
 #pragma unroll
-      for (int k = 0; k < QR; ++k)
-        if (lane + 32 * k < E) qraw[k] = qr[lane + 32 * k];
+      for (int g = 0; g < GR; ++g)
+#pragma unroll
+        for (int k = 0; k < QR; ++k)
+          qraw[g][k] = (g < snr && lane + 32 * k < E) ? qr[g * E + lane + 32 * k] : from_f32<T>(0.f);
       sapg0 = 0;
       sapg1 = -1;
       if (p.extra > 0 && st.len == st.raw + p.extra) {  // (a clamped length appends nothing)
@@ -487,10 +533,12 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
       __syncwarp();
       __threadfence_block();
       if (sid >= 0) {
-        float* row = sRows + r * E;
+        float* row = sRows + r * GR * E;
 #pragma unroll
-        for (int k = 0; k < QR; ++k)
-          if (lane + 32 * k < E) row[lane + 32 * k] = to_f32(qraw[k]);
+        for (int g = 0; g < GR; ++g)
+#pragma unroll
+          for (int k = 0; k < QR; ++k)
+            if (lane + 32 * k < E) row[g * E + lane + 32 * k] = to_f32(qraw[g][k]);
         if (fast) {
 #pragma unroll
           for (int k = 0; k < BR; ++k)
@@ -499,7 +547,11 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
         if (lane == 0) {
           e->id = sid;
           e->i = st.i;
-          e->h = st.h;
+          e->hk = shk;
+          e->h0 = sh0;
+          e->nrows = snr;
+          e->item = st.i * p.IH + st.ih;
+          e->gw = (sh0 == shk * p.G) ? 1 : 0;
           e->ntask = st.ntask;
           e->j = st.j;
           e->pg0 = st.pg0;
@@ -534,8 +586,8 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
     // ================================================================= merger
     // Combines the page states of each task in page order (so the result
     // does not depend on which warp streamed which page), frees the page
-    // slots and the queue entry, then writes the output row, or hands a split
-    // task's state to the finisher.
+    // slots and the queue entry, then writes the output rows, or hands a
+    // split task's states to the finisher.
     // First, while the feeder plans, this warp pulls the query rows and the
     // page table into L2 (the CTAs share the lines out), so that the loads of
     // every CTA's first task hit L2 instead of HBM.
@@ -555,15 +607,15 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
         prefetch_l2(a);
       }
       // and the first kDecodeWarmPages pages of item blockIdx.x (sequence
-      // blockIdx.x / H, head blockIdx.x % H): the first tasks' copies wait for
-      // three dependent round trips (lengths, plan and task, block ids), during
-      // which HBM would idle; these pages are read early in the call.
-      if ((long long)blockIdx.x < (long long)p.B * p.H && lane < kDecodeWarmPages && lane < p.pt_stride) {
-        const int i = (int)blockIdx.x / p.H, h = (int)blockIdx.x % p.H;
+      // blockIdx.x / IH): the first tasks' copies wait for three dependent
+      // round trips (lengths, plan and task, block ids), during which HBM
+      // would idle; these pages are read early in the call.
+      if ((long long)blockIdx.x < (long long)p.B * p.IH && lane < kDecodeWarmPages && lane < p.pt_stride) {
+        const int i = (int)blockIdx.x / p.IH, hk = ((int)blockIdx.x % p.IH) / p.NRG;
         const long long L = min((long long)__ldg(p.lens + i) + p.extra, p.pt_stride * (long long)p.page);
         const int blk = __ldg(p.page_table + (long long)i * p.pt_stride + lane);
         if ((long long)lane * p.page < L && blk >= 0 && blk < p.num_blocks) {
-          const long long off = ((long long)blk * p.H + h) * (long long)p.page_bytes;
+          const long long off = ((long long)blk * p.Hk + hk) * (long long)p.page_bytes;
           bulk_prefetch_l2(static_cast<const char*>(p.kc) + off, (uint32_t)p.page_bytes);
           bulk_prefetch_l2(static_cast<const char*>(p.vc) + off, (uint32_t)p.page_bytes);
         }
@@ -581,10 +633,17 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
       __threadfence_block();
       const int id = sQe[r].id;
       if (id < 0) break;
-      const int ei = sQe[r].i, eh = sQe[r].h, entask = sQe[r].ntask, ej = sQe[r].j, en = sQe[r].n,
-                est = sQe[r].start;
+      const int ei = sQe[r].i, eh0 = sQe[r].h0, enr = sQe[r].nrows, eitem = sQe[r].item, entask = sQe[r].ntask,
+                ej = sQe[r].j, en = sQe[r].n, est = sQe[r].start;
       const long long eslot = sQe[r].slot;
-      float M = -INFINITY, L = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
+      float M[GR], L[GR], o[GR][4];
+#pragma unroll
+      for (int g = 0; g < GR; ++g) {
+        M[g] = -INFINITY;
+        L[g] = 0.f;
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) o[g][cc] = 0.f;
+      }
       for (int gg = est; gg < est + en; ++gg) {
         const int ps = gg % R;
         if (!spin_until([&] { return sFlag[ps] == gg; }, sAbort, p.wait_ns)) {
@@ -592,33 +651,46 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
           break;
         }
         __threadfence_block();
-        const float* st = sPage + ps * (E + 4);
-        const float mp = st[E], lp = st[E + 1];
-        float a[4];
-        if (lane < Tile::kLanesPerKey) {
-          const float4 v4 = *reinterpret_cast<const float4*>(st + dg * 4);
-          a[0] = v4.x, a[1] = v4.y, a[2] = v4.z, a[3] = v4.w;
+        const float* stt = sPage + ps * GR * RS;
+        float mp[GR], lp[GR], a[GR][4];
+#pragma unroll
+        for (int g = 0; g < GR; ++g) {
+          mp[g] = stt[g * RS + E];
+          lp[g] = stt[g * RS + E + 1];
+          if (lane < Tile::kLanesPerKey) {
+            const float4 v4 = *reinterpret_cast<const float4*>(stt + g * RS + dg * 4);
+            a[g][0] = v4.x, a[g][1] = v4.y, a[g][2] = v4.z, a[g][3] = v4.w;
+          }
         }
         __syncwarp();
         if (lane == 0) *sMergedPages = gg + 1;  // slot ps is free
-        const float Mn = fmaxf(M, mp);
-        const float so = exp2_approx(M - Mn), sp = exp2_approx(mp - Mn);  // M = -inf: 0
-        L = fmaf(L, so, lp * sp);
-        if (lane < Tile::kLanesPerKey) {
 #pragma unroll
-          for (int cc = 0; cc < 4; ++cc) o[cc] = fmaf(o[cc], so, a[cc] * sp);
+        for (int g = 0; g < GR; ++g) {
+          const float Mn = fmaxf(M[g], mp[g]);
+          const float so = exp2_approx(M[g] - Mn), sp = exp2_approx(mp[g] - Mn);  // M = -inf: 0
+          L[g] = fmaf(L[g], so, lp[g] * sp);
+          if (lane < Tile::kLanesPerKey) {
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) o[g][cc] = fmaf(o[g][cc], so, a[g][cc] * sp);
+          }
+          M[g] = Mn;
         }
-        M = Mn;
       }
       if (!ok) break;
       __syncwarp();
       if (lane == 0) *sMerged = q + 1;  // the queue entry is free
       if (entask == 1) {
-        T* orow = obase + (long long)ei * p.out_stride + (long long)eh * E;
-        if (lane < Tile::kLanesPerKey) {
-          const float inv = L > 0.f ? 1.f / L : 0.f;
 #pragma unroll
-          for (int cc = 0; cc < 4; ++cc) orow[dg * 4 + cc] = from_f32<T>(L > 0.f ? o[cc] * inv : 0.f);
+        for (int g = 0; g < GR; ++g) {
+          if (g < enr) {
+            T* orow = obase + (long long)ei * p.out_stride + (long long)(eh0 + g) * E;
+            if (lane < Tile::kLanesPerKey) {
+              const float inv = L[g] > 0.f ? 1.f / L[g] : 0.f;
+#pragma unroll
+              for (int cc = 0; cc < 4; ++cc) orow[dg * 4 + cc] = from_f32<T>(L[g] > 0.f ? o[g][cc] * inv : 0.f);
+            }
+            if (p.lse && lane == 0) p.lse[(long long)ei * p.H + eh0 + g] = row_lse(M[g], L[g]);
+          }
         }
         continue;
       }
@@ -628,15 +700,25 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
         ok = false;
         break;
       }
-      if (lane < Tile::kLanesPerKey) *reinterpret_cast<float4*>(sFinO + fr * E + dg * 4) = make_float4(o[0], o[1], o[2], o[3]);
+      if (lane < Tile::kLanesPerKey) {
+#pragma unroll
+        for (int g = 0; g < GR; ++g)
+          *reinterpret_cast<float4*>(sFinO + (fr * GR + g) * E + dg * 4) =
+              make_float4(o[g][0], o[g][1], o[g][2], o[g][3]);
+      }
       if (lane == 0) {
         sFe[fr].i = ei;
-        sFe[fr].h = eh;
+        sFe[fr].h0 = eh0;
+        sFe[fr].nrows = enr;
+        sFe[fr].item = eitem;
         sFe[fr].ntask = entask;
         sFe[fr].j = ej;
         sFe[fr].slot = eslot;
-        sFe[fr].m = M;
-        sFe[fr].l = L;
+#pragma unroll
+        for (int g = 0; g < GR; ++g) {
+          sFe[fr].m[g] = M[g];
+          sFe[fr].l[g] = L[g];
+        }
       }
       __syncwarp();
       __threadfence_block();
@@ -662,68 +744,82 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
 
   if (w >= W + 2) {
     // ============================================================== finishers
-    // Split tasks: writes the task's partial (m, l, acc), takes the item's
-    // ticket, and the item's last task to finish merges all of its partials
-    // (in task order) into the output row. Finisher k takes the split tasks
-    // k, k + kDecodeFinishers, ... so that their global round trips overlap.
+    // Split tasks: writes the task's partials (m, l, acc of each row), takes
+    // the item's ticket, and the item's last task to finish merges all of its
+    // partials (in task order) into the output rows. Finisher k takes the
+    // split tasks k, k + kDecodeFinishers, ... so that their global round
+    // trips overlap.
     T* obase = static_cast<T*>(p.out);
+    constexpr int PS = E + 2;  // floats of one row's partial: m, l, acc[E]
     for (int f = w - (W + 2);; f += kDecodeFinishers) {
       const int fr = f % FQ;
       if (!spin_until([&] { return sFin[fr] == f; }, sAbort, p.wait_ns)) break;
       __threadfence_block();
       const int ei = sFe[fr].i;
       if (ei < 0) break;
-      const int eh = sFe[fr].h, entask = sFe[fr].ntask, ej = sFe[fr].j;
+      const int eh0 = sFe[fr].h0, enr = sFe[fr].nrows, eitem = sFe[fr].item, entask = sFe[fr].ntask,
+                ej = sFe[fr].j;
       const long long eslot = sFe[fr].slot;
-      const float M = sFe[fr].m, L = sFe[fr].l;
-      float o[4] = {0.f, 0.f, 0.f, 0.f};
-      if (lane < Tile::kLanesPerKey) {
-        const float4 v4 = *reinterpret_cast<const float4*>(sFinO + fr * E + dg * 4);
-        o[0] = v4.x, o[1] = v4.y, o[2] = v4.z, o[3] = v4.w;
+      float M[GR], L[GR], o[GR][4];
+#pragma unroll
+      for (int g = 0; g < GR; ++g) {
+        M[g] = sFe[fr].m[g];
+        L[g] = sFe[fr].l[g];
+        if (lane < Tile::kLanesPerKey) {
+          const float4 v4 = *reinterpret_cast<const float4*>(sFinO + (fr * GR + g) * E + dg * 4);
+          o[g][0] = v4.x, o[g][1] = v4.y, o[g][2] = v4.z, o[g][3] = v4.w;
+        }
       }
       __syncwarp();
       if (lane == 0) sFinAck[fr] = f;
-      float* slot = p.partial + eslot * (E + 2);
-      if (lane < Tile::kLanesPerKey) {
+      float* slot = p.partial + eslot * (GR * PS);
 #pragma unroll
-        for (int cc = 0; cc < 4; ++cc) slot[2 + dg * 4 + cc] = o[cc];
+      for (int g = 0; g < GR; ++g) {
+        if (lane < Tile::kLanesPerKey) {
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) slot[g * PS + 2 + dg * 4 + cc] = o[g][cc];
+        }
+        if (lane == 0) {
+          slot[g * PS] = M[g];
+          slot[g * PS + 1] = L[g];
+        }
       }
-      if (lane == 0) {
-        slot[0] = M;
-        slot[1] = L;
-      }
-      // the ticket is an acquire-release atomic: it releases the partial (every
-      // lane's writes, ordered before it by the warp barrier) and, for the
-      // last task, acquires the other tasks' partials
+      // the ticket is an acquire-release atomic: it releases the partials
+      // (every lane's writes, ordered before it by the warp barrier) and, for
+      // the last task, acquires the other tasks' partials
       __syncwarp();
       int ticket = 0;
-      int* tk = p.tickets + (long long)ei * p.H + eh;
+      int* tk = p.tickets + eitem;
       if (lane == 0) ticket = atom_add_acq_rel_gpu(tk, 1);
       ticket = __shfl_sync(0xffffffffu, ticket, 0);
       if (ticket != entask - 1) continue;
       __syncwarp();
-      const float* first = p.partial + (eslot - ej) * (E + 2);
-      float MM = -INFINITY;
-      for (int jj = lane; jj < entask; jj += 32) MM = fmaxf(MM, __ldcg(first + (long long)jj * (E + 2)));
-      MM = warp_max(MM);
-      float LL = 0.f, oo[4] = {0.f, 0.f, 0.f, 0.f};
-      if (MM != -INFINITY) {
+      const float* first = p.partial + (eslot - ej) * (GR * PS);
+      for (int g = 0; g < enr; ++g) {
+        const float* fg = first + g * PS;
+        float MM = -INFINITY;
+        for (int jj = lane; jj < entask; jj += 32) MM = fmaxf(MM, __ldcg(fg + (long long)jj * (GR * PS)));
+        MM = warp_max(MM);
+        float LL = 0.f, oo[4] = {0.f, 0.f, 0.f, 0.f};
+        if (MM != -INFINITY) {
 #pragma unroll 4
-        for (int jj = 0; jj < entask; ++jj) {  // task order, every lane alike
-          const float* ps = first + (long long)jj * (E + 2);
-          const float wt = exp2_approx(__ldcg(ps) - MM);
-          LL = fmaf(__ldcg(ps + 1), wt, LL);
-          if (lane < Tile::kLanesPerKey) {
+          for (int jj = 0; jj < entask; ++jj) {  // task order, every lane alike
+            const float* ps = fg + (long long)jj * (GR * PS);
+            const float wt = exp2_approx(__ldcg(ps) - MM);
+            LL = fmaf(__ldcg(ps + 1), wt, LL);
+            if (lane < Tile::kLanesPerKey) {
 #pragma unroll
-            for (int cc = 0; cc < 4; ++cc) oo[cc] = fmaf(__ldcg(ps + 2 + dg * 4 + cc), wt, oo[cc]);
+              for (int cc = 0; cc < 4; ++cc) oo[cc] = fmaf(__ldcg(ps + 2 + dg * 4 + cc), wt, oo[cc]);
+            }
           }
         }
-      }
-      T* orow = obase + (long long)ei * p.out_stride + (long long)eh * E;
-      if (lane < Tile::kLanesPerKey) {
-        const float inv = LL > 0.f ? 1.f / LL : 0.f;
+        T* orow = obase + (long long)ei * p.out_stride + (long long)(eh0 + g) * E;
+        if (lane < Tile::kLanesPerKey) {
+          const float inv = LL > 0.f ? 1.f / LL : 0.f;
 #pragma unroll
-        for (int cc = 0; cc < 4; ++cc) orow[dg * 4 + cc] = from_f32<T>(LL > 0.f ? oo[cc] * inv : 0.f);
+          for (int cc = 0; cc < 4; ++cc) orow[dg * 4 + cc] = from_f32<T>(LL > 0.f ? oo[cc] * inv : 0.f);
+        }
+        if (p.lse && lane == 0) p.lse[(long long)ei * p.H + eh0 + g] = row_lse(MM, LL);
       }
       if (lane == 0) *tk = 0;  // ready for the next call
     }
@@ -744,7 +840,7 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
   bool pdone = false;         // the end marker was reached
   int cq = 0;                 // queue position the walk is at
   int c_start = 0, c_n = -1;  // its pages in the stream (c_n < 0: not read)
-  int c_i = 0, c_h = 0, c_pg0 = 0, c_staged = 0;
+  int c_i = 0, c_hk = 0, c_pg0 = 0, c_staged = 0;
   unsigned pidx = 0, cidx = 0;  // pages produced / consumed
   auto produce = [&]() {
     while (!pdone && pidx - cidx < (unsigned)p.stages) {
@@ -764,7 +860,7 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
           if (sSeq[r] != cq) return;  // not published yet: keep the claim pending
           __threadfence_block();
           const int id = sQe[r].id, st = sQe[r].start, n = sQe[r].n;
-          const int ii = sQe[r].i, hh = sQe[r].h, pg0 = sQe[r].pg0, stg = sQe[r].staged;
+          const int ii = sQe[r].i, hh = sQe[r].hk, pg0 = sQe[r].pg0, stg = sQe[r].staged;
           __threadfence_block();
           if (sSeq[r] != cq) continue;  // rewritten while read: look again
           if (id < 0) {
@@ -774,7 +870,7 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
           c_start = st;
           c_n = n;
           c_i = ii;
-          c_h = hh;
+          c_hk = hh;
           c_pg0 = pg0;
           c_staged = stg;
         }
@@ -797,7 +893,7 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
             blk = 0;
           }
         }
-        const long long off = ((long long)blk * p.H + c_h) * (long long)p.page_bytes;
+        const long long off = ((long long)blk * p.Hk + c_hk) * (long long)p.page_bytes;
         mbar_arrive_expect_tx(&sBar[s], (uint32_t)(2 * p.page_bytes));
         fence_proxy_async_smem();
         bulk_g2s(stage, kc + off, (uint32_t)p.page_bytes, &sBar[s], policy);
@@ -809,15 +905,20 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
     }
   };
 
-  // ---- consumer: each page on its own (m, l, acc), deposited in the page
-  // slot of its stream position for the merger
+  // ---- consumer: each page on its own (m, l, acc) per row, deposited in the
+  // page slot of its stream position for the merger
   bool failed = false;    // a bounded wait gave up: stop (the other warps stop too)
   unsigned fail_idx = 0;  // the first page not waited for
   int cur = -1;           // task position whose fields are loaded
   struct {
-    int i, h, len, raw, apg0, apg1;
-  } t = {0, 0, 0, 0, 0, -1};
+    int i, hk, len, raw, apg0, apg1, gw;
+  } t = {0, 0, 0, 0, 0, -1, 0};
   const float* sQ = sRows;
+  // K.q accumulation chains per row: four for one row, fewer as the rows
+  // themselves give independent chains
+  constexpr int CH = GR >= 4 ? 1 : 4 / GR;
+  constexpr int NS = kDecodeMaxPage / 32;
+  constexpr int UQK = GR == 1 ? 8 : 4;  // unroll of the K-row loops
   for (;;) {
     produce();
     if (pidx == cidx) {
@@ -838,16 +939,22 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
       const int r = tag.x % QD;
       cur = tag.x;
       t.i = sQe[r].i;
-      t.h = sQe[r].h;
+      t.hk = sQe[r].hk;
       t.len = sQe[r].len;
       t.raw = sQe[r].raw;
       t.apg0 = sQe[r].apg0;
       t.apg1 = sQe[r].apg1;
-      sQ = sRows + r * E;
+      t.gw = sQe[r].gw;
+      sQ = sRows + r * GR * E;
     }
-    const float4* sQ4 = reinterpret_cast<const float4*>(sQ);
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    float m, lpart = 0.f;
+    float acc[GR][4];
+    float m[GR], lpart[GR];
+#pragma unroll
+    for (int gr = 0; gr < GR; ++gr) {
+      lpart[gr] = 0.f;
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) acc[gr][cc] = 0.f;
+    }
     {
       const uint32_t parity = (cidx / (unsigned)p.stages) & 1u;
       if (!decode_wait(&sBar[s], parity, sAbort, p.wait_ns)) {
@@ -861,17 +968,17 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
       if (pg >= t.apg0 && pg <= t.apg1) {
         // appended tokens in this page: into the staged page (shared) and the
         // cache (global), K transposed as the page layout wants, V as rows.
-        // A page is streamed by exactly one warp in a call, so each token is
-        // written once.
+        // The first item of the KV head writes the cache: a page is streamed
+        // by exactly one warp per item in a call, so each token is written once.
         const int lo = max(t.raw - pg * p.page, 0), hi = min(t.raw + p.extra - pg * p.page, p.page);
         int gblk = __ldg(p.page_table + (long long)t.i * p.pt_stride + pg);
-        if (gblk < 0 || gblk >= p.num_blocks) gblk = -1;
+        if (gblk < 0 || gblk >= p.num_blocks || !t.gw) gblk = -1;
         T* sKe = reinterpret_cast<T*>(stage);
         T* sV = reinterpret_cast<T*>(stage + p.kslot_bytes);
-        const long long pbase = gblk >= 0 ? ((long long)gblk * p.H + t.h) * (long long)p.page * E : 0;
+        const long long pbase = gblk >= 0 ? ((long long)gblk * p.Hk + t.hk) * (long long)p.page * E : 0;
         T* gK = static_cast<T*>(const_cast<void*>(p.kc)) + pbase;
         T* gV = static_cast<T*>(const_cast<void*>(p.vc)) + pbase;
-        const long long rowbase = (long long)t.i * p.kv_stride + (long long)t.h * E;
+        const long long rowbase = (long long)t.i * p.kv_stride + (long long)t.hk * E;
         for (int idx = lane; idx < (hi - lo) * E; idx += 32) {
           const int tt = lo + idx / E, d = idx % E;
           const long long src = rowbase + (long long)(pg * p.page + tt - t.raw) * p.kv_tstride + d;
@@ -888,88 +995,139 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
         __syncwarp();
       }
 
-      // ---- Q.K^T for the page's ntok keys
+      // ---- Q.K^T for the page's ntok keys, every row
       const uint32_t* sK = reinterpret_cast<const uint32_t*>(stage);
       const int nsteps = (ntok + 31) >> 5;
-      float x[kDecodeMaxPage / 32];
+      float x[GR][NS];
+      float mc[GR];
 #pragma unroll
-      for (int st = 0; st < kDecodeMaxPage / 32; ++st) x[st] = -INFINITY;
-      float mc = -INFINITY;
+      for (int gr = 0; gr < GR; ++gr) {
+        mc[gr] = -INFINITY;
+#pragma unroll
+        for (int stp = 0; stp < NS; ++stp) x[gr][stp] = -INFINITY;
+      }
       if (p.page == 16) {
         // a 16-key page: lanes t and 16+t share key t, each half-warp takes
         // every other K row (conflict-free: banks 16*half + t)
         const int tk = lane & 15, hh = lane >> 4;
         const uint32_t* kp = sK + tk;
-        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+        float a[GR][CH];
+#pragma unroll
+        for (int gr = 0; gr < GR; ++gr)
+#pragma unroll
+          for (int c = 0; c < CH; ++c) a[gr][c] = 0.f;
         if constexpr (Tile::kBF) {
-          const float2* sQ2 = reinterpret_cast<const float2*>(sQ);
-#pragma unroll 8
+#pragma unroll UQK
           for (int r = hh; r < Tile::kRows; r += 4) {
             const uint32_t w0 = kp[r * 16];
             const uint32_t w1 = kp[(r + 2) * 16];
-            const float2 q0 = sQ2[r], q1 = sQ2[r + 2];
-            a0 = fmaf(bf16_lo(w0), q0.x, a0);
-            a1 = fmaf(bf16_hi(w0), q0.y, a1);
-            a2 = fmaf(bf16_lo(w1), q1.x, a2);
-            a3 = fmaf(bf16_hi(w1), q1.y, a3);
+            const float k0 = bf16_lo(w0), k1 = bf16_hi(w0), k2 = bf16_lo(w1), k3 = bf16_hi(w1);
+#pragma unroll
+            for (int gr = 0; gr < GR; ++gr) {
+              const float2* q2 = reinterpret_cast<const float2*>(sQ + gr * E);
+              const float2 q0 = q2[r], q1 = q2[r + 2];
+              a[gr][0 % CH] = fmaf(k0, q0.x, a[gr][0 % CH]);
+              a[gr][1 % CH] = fmaf(k1, q0.y, a[gr][1 % CH]);
+              a[gr][2 % CH] = fmaf(k2, q1.x, a[gr][2 % CH]);
+              a[gr][3 % CH] = fmaf(k3, q1.y, a[gr][3 % CH]);
+            }
           }
         } else {
           const float* kf = reinterpret_cast<const float*>(kp);
-#pragma unroll 8
+#pragma unroll UQK
           for (int r = hh; r < Tile::kRows; r += 8) {
-            a0 = fmaf(kf[r * 16], sQ[r], a0);
-            a1 = fmaf(kf[(r + 2) * 16], sQ[r + 2], a1);
-            a2 = fmaf(kf[(r + 4) * 16], sQ[r + 4], a2);
-            a3 = fmaf(kf[(r + 6) * 16], sQ[r + 6], a3);
+            const float k0 = kf[r * 16], k1 = kf[(r + 2) * 16], k2 = kf[(r + 4) * 16], k3 = kf[(r + 6) * 16];
+#pragma unroll
+            for (int gr = 0; gr < GR; ++gr) {
+              const float* qf = sQ + gr * E;
+              a[gr][0 % CH] = fmaf(k0, qf[r], a[gr][0 % CH]);
+              a[gr][1 % CH] = fmaf(k1, qf[r + 2], a[gr][1 % CH]);
+              a[gr][2 % CH] = fmaf(k2, qf[r + 4], a[gr][2 % CH]);
+              a[gr][3 % CH] = fmaf(k3, qf[r + 6], a[gr][3 % CH]);
+            }
           }
         }
-        float logit = (a0 + a1) + (a2 + a3);
-        logit += __shfl_xor_sync(0xffffffffu, logit, 16);
-        x[0] = (tk < ntok && hh == 0) ? logit * p.c : -INFINITY;
-        mc = x[0];
+#pragma unroll
+        for (int gr = 0; gr < GR; ++gr) {
+          float logit;
+          if constexpr (CH == 4)
+            logit = (a[gr][0] + a[gr][1]) + (a[gr][2] + a[gr][3]);
+          else if constexpr (CH == 2)
+            logit = a[gr][0] + a[gr][1];
+          else
+            logit = a[gr][0];
+          logit += __shfl_xor_sync(0xffffffffu, logit, 16);
+          x[gr][0] = (tk < ntok && hh == 0) ? logit * p.c : -INFINITY;
+          mc[gr] = x[gr][0];
+        }
       } else {
 #pragma unroll
-        for (int st = 0; st < kDecodeMaxPage / 32; ++st) {
-          if (st < nsteps) {
-            const int j = st * 32 + lane;
+        for (int stp = 0; stp < NS; ++stp) {
+          if (stp < nsteps) {
+            const int j = stp * 32 + lane;
             const uint32_t* kp = sK + min(j, ntok - 1);
-            float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+            float a[GR][CH];
+#pragma unroll
+            for (int gr = 0; gr < GR; ++gr)
+#pragma unroll
+              for (int c = 0; c < CH; ++c) a[gr][c] = 0.f;
             if constexpr (Tile::kBF) {
-#pragma unroll 8
+#pragma unroll UQK
               for (int r = 0; r < Tile::kRows; r += 2) {
                 const uint32_t w0 = kp[r * p.page];
                 const uint32_t w1 = kp[(r + 1) * p.page];
-                const float4 qq = sQ4[r >> 1];
-                a0 = fmaf(bf16_lo(w0), qq.x, a0);
-                a1 = fmaf(bf16_hi(w0), qq.y, a1);
-                a2 = fmaf(bf16_lo(w1), qq.z, a2);
-                a3 = fmaf(bf16_hi(w1), qq.w, a3);
+                const float k0 = bf16_lo(w0), k1 = bf16_hi(w0), k2 = bf16_lo(w1), k3 = bf16_hi(w1);
+#pragma unroll
+                for (int gr = 0; gr < GR; ++gr) {
+                  const float4 qq = reinterpret_cast<const float4*>(sQ + gr * E)[r >> 1];
+                  a[gr][0 % CH] = fmaf(k0, qq.x, a[gr][0 % CH]);
+                  a[gr][1 % CH] = fmaf(k1, qq.y, a[gr][1 % CH]);
+                  a[gr][2 % CH] = fmaf(k2, qq.z, a[gr][2 % CH]);
+                  a[gr][3 % CH] = fmaf(k3, qq.w, a[gr][3 % CH]);
+                }
               }
             } else {
               const float* kf = reinterpret_cast<const float*>(kp);
-#pragma unroll 8
+#pragma unroll UQK
               for (int r = 0; r < Tile::kRows; r += 4) {
-                const float4 qq = sQ4[r >> 2];
-                a0 = fmaf(kf[r * p.page], qq.x, a0);
-                a1 = fmaf(kf[(r + 1) * p.page], qq.y, a1);
-                a2 = fmaf(kf[(r + 2) * p.page], qq.z, a2);
-                a3 = fmaf(kf[(r + 3) * p.page], qq.w, a3);
+                const float k0 = kf[r * p.page], k1 = kf[(r + 1) * p.page], k2 = kf[(r + 2) * p.page],
+                            k3 = kf[(r + 3) * p.page];
+#pragma unroll
+                for (int gr = 0; gr < GR; ++gr) {
+                  const float4 qq = reinterpret_cast<const float4*>(sQ + gr * E)[r >> 2];
+                  a[gr][0 % CH] = fmaf(k0, qq.x, a[gr][0 % CH]);
+                  a[gr][1 % CH] = fmaf(k1, qq.y, a[gr][1 % CH]);
+                  a[gr][2 % CH] = fmaf(k2, qq.z, a[gr][2 % CH]);
+                  a[gr][3 % CH] = fmaf(k3, qq.w, a[gr][3 % CH]);
+                }
               }
             }
-            const float logit = (a0 + a1) + (a2 + a3);
-            x[st] = (j < ntok) ? logit * p.c : -INFINITY;
-            mc = fmaxf(mc, x[st]);
+#pragma unroll
+            for (int gr = 0; gr < GR; ++gr) {
+              float logit;
+              if constexpr (CH == 4)
+                logit = (a[gr][0] + a[gr][1]) + (a[gr][2] + a[gr][3]);
+              else if constexpr (CH == 2)
+                logit = a[gr][0] + a[gr][1];
+              else
+                logit = a[gr][0];
+              x[gr][stp] = (j < ntok) ? logit * p.c : -INFINITY;
+              mc[gr] = fmaxf(mc[gr], x[gr][stp]);
+            }
           }
         }
       }
-      // ---- softmax of the page on its own maximum
-      m = warp_max(mc);
+      // ---- softmax of the page on its own maximum, per row
 #pragma unroll
-      for (int st = 0; st < kDecodeMaxPage / 32; ++st) {
-        if (st < nsteps) {
-          const float pr = exp2_approx(x[st] - m);
-          sP[st * 32 + lane] = pr;
-          lpart += pr;
+      for (int gr = 0; gr < GR; ++gr) {
+        m[gr] = warp_max(mc[gr]);
+#pragma unroll
+        for (int stp = 0; stp < NS; ++stp) {
+          if (stp < nsteps) {
+            const float pr = exp2_approx(x[gr][stp] - m[gr]);
+            sP[gr * kDecodeMaxPage + stp * 32 + lane] = pr;
+            lpart[gr] += pr;
+          }
         }
       }
       __syncwarp();
@@ -978,35 +1136,46 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
       if constexpr (Tile::kBF) {
 #pragma unroll 4
         for (int tt = tg; tt < ntok; tt += Tile::kKeysPerStep) {
-          const float pj = sP[tt];
           const uint2 wv = *reinterpret_cast<const uint2*>(vb + tt * vrow_words + dg * 2);
-          acc[0] = fmaf(pj, bf16_lo(wv.x), acc[0]);
-          acc[1] = fmaf(pj, bf16_hi(wv.x), acc[1]);
-          acc[2] = fmaf(pj, bf16_lo(wv.y), acc[2]);
-          acc[3] = fmaf(pj, bf16_hi(wv.y), acc[3]);
+          const float v0 = bf16_lo(wv.x), v1 = bf16_hi(wv.x), v2 = bf16_lo(wv.y), v3 = bf16_hi(wv.y);
+#pragma unroll
+          for (int gr = 0; gr < GR; ++gr) {
+            const float pj = sP[gr * kDecodeMaxPage + tt];
+            acc[gr][0] = fmaf(pj, v0, acc[gr][0]);
+            acc[gr][1] = fmaf(pj, v1, acc[gr][1]);
+            acc[gr][2] = fmaf(pj, v2, acc[gr][2]);
+            acc[gr][3] = fmaf(pj, v3, acc[gr][3]);
+          }
         }
       } else {
 #pragma unroll 4
         for (int tt = tg; tt < ntok; tt += Tile::kKeysPerStep) {
-          const float pj = sP[tt];
           const float4 wv = *reinterpret_cast<const float4*>(vb + tt * vrow_words + dg * 4);
-          acc[0] = fmaf(pj, wv.x, acc[0]);
-          acc[1] = fmaf(pj, wv.y, acc[1]);
-          acc[2] = fmaf(pj, wv.z, acc[2]);
-          acc[3] = fmaf(pj, wv.w, acc[3]);
+#pragma unroll
+          for (int gr = 0; gr < GR; ++gr) {
+            const float pj = sP[gr * kDecodeMaxPage + tt];
+            acc[gr][0] = fmaf(pj, wv.x, acc[gr][0]);
+            acc[gr][1] = fmaf(pj, wv.y, acc[gr][1]);
+            acc[gr][2] = fmaf(pj, wv.z, acc[gr][2]);
+            acc[gr][3] = fmaf(pj, wv.w, acc[gr][3]);
+          }
         }
       }
       __syncwarp();  // every lane is done with stage s
       ++cidx;
     }
     produce();  // the stage is free: refill it before depositing
-    // ---- deposit the page's state in slot tag.z % R once the merger is past
+    // ---- deposit the page's states in slot tag.z % R once the merger is past
     // the page that held it before
-    const float l = warp_sum(lpart);
+    float l[GR];
 #pragma unroll
-    for (int o = Tile::kLanesPerKey; o < 32; o <<= 1) {
+    for (int gr = 0; gr < GR; ++gr) {
+      l[gr] = warp_sum(lpart[gr]);
 #pragma unroll
-      for (int cc = 0; cc < 4; ++cc) acc[cc] += __shfl_xor_sync(0xffffffffu, acc[cc], o);
+      for (int o = Tile::kLanesPerKey; o < 32; o <<= 1) {
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) acc[gr][cc] += __shfl_xor_sync(0xffffffffu, acc[gr][cc], o);
+      }
     }
     const int gz = tag.z;
     if (!spin_until([&] { return *sMergedPages > gz - R; }, sAbort, p.wait_ns)) {
@@ -1014,11 +1183,16 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
       fail_idx = cidx;
       break;
     }
-    float* slot = sPage + (gz % R) * (E + 4);
-    if (lane < Tile::kLanesPerKey) *reinterpret_cast<float4*>(slot + dg * 4) = make_float4(acc[0], acc[1], acc[2], acc[3]);
-    if (lane == 0) {
-      slot[E] = m;
-      slot[E + 1] = l;
+    float* slot = sPage + (gz % R) * GR * RS;
+#pragma unroll
+    for (int gr = 0; gr < GR; ++gr) {
+      if (lane < Tile::kLanesPerKey)
+        *reinterpret_cast<float4*>(slot + gr * RS + dg * 4) =
+            make_float4(acc[gr][0], acc[gr][1], acc[gr][2], acc[gr][3]);
+      if (lane == 0) {
+        slot[gr * RS + E] = m[gr];
+        slot[gr * RS + E + 1] = l[gr];
+      }
     }
     __syncwarp();
     __threadfence_block();

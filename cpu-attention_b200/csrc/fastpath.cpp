@@ -1,8 +1,9 @@
 // The decode and prefill entries' host path in C++: the same argument checks
 // as cpu_attention/_native.py::decode and ::flash (which mirror
 // `_C.mojo:87-171` and `:232-316`), done on at::Tensor fields instead of
-// Python attribute calls, then the C ABI call (ca_decode / ca_decode_append /
-// ca_flash) on the device's current stream. A decode step is short enough
+// Python attribute calls, then the C ABI call (ca_decode_ex / ca_flash_ex) on
+// the device's current stream. Varlen prefill and prefill log-sum-exp take the
+// Python path. A decode step is short enough
 // (tens of µs) that the Python checks and the ctypes call were the larger part
 // of an end-to-end step's host time.
 //
@@ -64,10 +65,19 @@ bool int_vector(const at::Tensor& t, at::ScalarType dt, int64_t n) {
   return t.dim() == 1 && t.scalar_type() == dt && t.size(0) == n && t.is_contiguous();
 }
 
+// lse: absent, or float32 of `shape`, contiguous, on `device`
+bool lse_ok(const c10::optional<at::Tensor>& lse, at::IntArrayRef shape, const c10::Device& device) {
+  if (!lse) return true;
+  const at::Tensor& t = *lse;
+  return t.is_cuda() && t.device() == device && t.scalar_type() == at::kFloat && t.sizes() == shape &&
+         t.is_contiguous();
+}
+
 // Returns the output tensor, or None when the call is declined.
 py::object decode(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& vc, const c10::optional<at::Tensor>& k,
                   const c10::optional<at::Tensor>& v, const c10::optional<at::Tensor>& slots, const at::Tensor& lens,
-                  const at::Tensor& pt, const c10::optional<double>& scale, const c10::optional<at::Tensor>& dst) {
+                  const at::Tensor& pt, const c10::optional<double>& scale, const c10::optional<at::Tensor>& dst,
+                  const c10::optional<at::Tensor>& lse) {
   // one CUDA device for every tensor
   if (!q.is_cuda()) return py::none();
   const auto device = q.device();
@@ -80,29 +90,33 @@ py::object decode(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& v
   const int64_t b = q.size(0), heads = q.size(-2), hd = q.size(-1);
   const int dt = dtype_code(q.scalar_type());
   if (dt < 0 || !head_dim_ok(hd) || !rows_ok(q, hd)) return py::none();
-  // caches: [blocks, heads, page, dim], contiguous, matching, page % 16 == 0 (`_C.mojo:74-80`)
+  // caches: [blocks, kv_heads, page, dim], contiguous, matching, page % 16 == 0
+  // (`_C.mojo:74-80`); kv_heads divides heads
   if (kc.dim() != 4 || vc.sizes() != kc.sizes()) return py::none();
-  if (kc.scalar_type() != q.scalar_type() || vc.scalar_type() != q.scalar_type() || kc.size(1) != heads ||
-      kc.size(3) != hd || kc.size(2) <= 0 || kc.size(2) % 16 || !kc.is_contiguous() || !vc.is_contiguous())
+  const int64_t kvh = kc.size(1);
+  if (kvh < 1 || heads % kvh) return py::none();
+  if (kc.scalar_type() != q.scalar_type() || vc.scalar_type() != q.scalar_type() || kc.size(3) != hd ||
+      kc.size(2) <= 0 || kc.size(2) % 16 || !kc.is_contiguous() || !vc.is_contiguous())
     return py::none();
   const int64_t page = kc.size(2);
   if (pt.dim() != 2 || pt.scalar_type() != at::kInt || pt.size(0) != b || !pt.is_contiguous()) return py::none();
   if (!int_vector(lens, at::kInt, b)) return py::none();
   const bool store = k.has_value();
-  int64_t n_new = 1;
+  int64_t n_new = 0;
   if (store) {
     const at::Tensor& kk = *k;
-    const bool multi = nd == 4 && !slots && kk.dim() == 4 && kk.size(0) == b && kk.size(1) > 1 &&
-                       kk.size(2) == heads && kk.size(3) == hd;
-    if (!v || (kk.sizes() != q.sizes() && !multi) || v->sizes() != kk.sizes() || v->strides() != kk.strides())
+    if (!v || kk.dim() != nd || v->sizes() != kk.sizes() || v->strides() != kk.strides()) return py::none();
+    if (kk.size(0) != b || kk.size(-2) != kvh || kk.size(-1) != hd || (nd == 4 && kk.size(1) < 1))
       return py::none();
-    if (kk.scalar_type() != q.scalar_type() || v->scalar_type() != q.scalar_type() || !rows_ok(kk, hd))
+    n_new = nd == 4 ? kk.size(1) : 1;
+    if (kk.scalar_type() != q.scalar_type() || v->scalar_type() != q.scalar_type() || !rows_ok(kk, hd) ||
+        (slots && n_new != 1))
       return py::none();
-    if (multi) n_new = kk.size(1);
   } else if (v) {
     return py::none();
   }
   if (slots && !(store && int_vector(*slots, at::kLong, b))) return py::none();
+  if (!lse_ok(lse, {b, heads}, device)) return py::none();
   at::Tensor out;
   if (!dst) {
     out = at::empty(q.sizes(), q.options());
@@ -119,38 +133,32 @@ py::object decode(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& v
   cudaStream_t stream = c10::cuda::getCurrentCUDAStream(dev).stream();
   at::Tensor ws = workspace(dev, (uintptr_t)stream, (int64_t)need);
   const float sc = scale ? (float)*scale : std::nanf("");
-  int rc;
-  if (n_new > 1) {
-    rc = ca_decode_append(q.data_ptr(), q.stride(0), kc.data_ptr(), vc.data_ptr(), kc.size(0), k->data_ptr(),
-                          v->data_ptr(), k->stride(0), k->stride(1), n_new, lens.data_ptr<int32_t>(),
-                          pt.data_ptr<int32_t>(), pt.size(1), out.data_ptr(), b, heads, hd, page, dt, sc,
-                          ws.data_ptr(), (size_t)ws.numel(), stream);
-  } else {
-    rc = ca_decode(q.data_ptr(), q.stride(0), kc.data_ptr(), vc.data_ptr(), kc.size(0),
-                   store ? k->data_ptr() : nullptr, store ? v->data_ptr() : nullptr, store ? k->stride(0) : 0,
-                   slots ? slots->data_ptr<int64_t>() : nullptr, lens.data_ptr<int32_t>(), pt.data_ptr<int32_t>(),
-                   pt.size(1), out.data_ptr(), b, heads, hd, page, dt, sc, ws.data_ptr(), (size_t)ws.numel(),
-                   stream);
-  }
+  const int rc = ca_decode_ex(q.data_ptr(), q.stride(0), kc.data_ptr(), vc.data_ptr(), kc.size(0),
+                             store ? k->data_ptr() : nullptr, store ? v->data_ptr() : nullptr,
+                             store ? k->stride(0) : 0, store && nd == 4 ? k->stride(1) : 0, n_new,
+                             slots ? slots->data_ptr<int64_t>() : nullptr, lens.data_ptr<int32_t>(),
+                             pt.data_ptr<int32_t>(), pt.size(1), out.data_ptr(),
+                             lse ? lse->data_ptr<float>() : nullptr, b, heads, kvh, hd, page, dt, sc, ws.data_ptr(),
+                             (size_t)ws.numel(), stream);
   if (rc == CA_ECUDA) throw std::runtime_error(std::string("cpu_attention: ") + ca_last_cuda_error());
   if (rc != CA_OK) return py::none();
   return py::cast(out);
 }
 
-// flash_attn_func over q/k/v [batch, seq, heads, dim] (MHA, dims contiguous):
-// the checks of cpu_attention/_native.py::flash (`_C.mojo:232-316`), then
-// ca_flash. Returns the output, or None when declined.
+// flash_attn_func over q [batch, seq, heads, dim] and k/v [batch, seq_k,
+// kv_heads, dim] (kv_heads divides heads; dims contiguous): the checks of
+// cpu_attention/_native.py::flash (`_C.mojo:232-316`), then ca_flash_ex.
+// Returns the output, or None when declined.
 py::object flash(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const c10::optional<double>& scale,
                  bool causal) {
   if (!q.is_cuda()) return py::none();
   const auto device = q.device();
   if (!k.is_cuda() || k.device() != device || !v.is_cuda() || v.device() != device) return py::none();
   if (q.dim() != 4 || k.dim() != 4 || v.dim() != 4) return py::none();
-  const int64_t b = q.size(0), sq = q.size(1), heads = q.size(2), hd = q.size(3), sk = k.size(1);
+  const int64_t b = q.size(0), sq = q.size(1), heads = q.size(2), hd = q.size(3), sk = k.size(1), kvh = k.size(2);
   const int dt = dtype_code(q.scalar_type());
-  if (dt < 0 || !head_dim_ok(hd) || sq < 1 || sk < 1) return py::none();
-  if (k.size(0) != b || k.size(2) != heads || k.size(3) != hd || k.scalar_type() != q.scalar_type() ||
-      v.scalar_type() != q.scalar_type())
+  if (dt < 0 || !head_dim_ok(hd) || sq < 1 || sk < 1 || kvh < 1 || heads % kvh) return py::none();
+  if (k.size(0) != b || k.size(3) != hd || k.scalar_type() != q.scalar_type() || v.scalar_type() != q.scalar_type())
     return py::none();
   if (v.sizes() != k.sizes() || q.stride(3) != 1 || k.stride(3) != 1 || v.stride(3) != 1) return py::none();
   at::Tensor out = at::empty({b, sq, heads, hd}, q.options().memory_format(at::MemoryFormat::Contiguous));
@@ -163,8 +171,9 @@ py::object flash(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, 
   const int64_t ks[3] = {k.stride(0), k.stride(1), k.stride(2)};
   const int64_t vs[3] = {v.stride(0), v.stride(1), v.stride(2)};
   const float sc = scale ? (float)*scale : std::nanf("");
-  const int rc = ca_flash(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), b, sq, sk, heads, hd, qs, ks, vs,
-                          sc, causal ? 1 : 0, dt, static_cast<int32_t*>(ws.data_ptr()), stream);
+  const int rc = ca_flash_ex(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), nullptr, b, sq, sk, heads, kvh,
+                             hd, qs, ks, vs, nullptr, nullptr, 0, 0, sc, causal ? 1 : 0, dt,
+                             static_cast<int32_t*>(ws.data_ptr()), stream);
   if (rc == CA_ECUDA) throw std::runtime_error(std::string("cpu_attention: ") + ca_last_cuda_error());
   if (rc != CA_OK) return py::none();
   return py::cast(out);
@@ -176,7 +185,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "cpu_attention's decode host path in C++ (argument checks and the C ABI call)";
   m.def("decode", &decode, "paged decode; the output tensor, or None when declined", py::arg("q"), py::arg("k_cache"),
         py::arg("v_cache"), py::arg("k"), py::arg("v"), py::arg("slots"), py::arg("lens"), py::arg("page_table"),
-        py::arg("scale"), py::arg("dst"));
+        py::arg("scale"), py::arg("dst"), py::arg("lse") = py::none());
   m.def("flash", &flash, "dense prefill; the output tensor, or None when declined", py::arg("q"), py::arg("k"),
         py::arg("v"), py::arg("scale"), py::arg("causal"));
   m.def("workspace", &py_workspace, "the workspace tensor of (device, stream), at least nbytes long",

@@ -23,11 +23,51 @@ struct FlashParams {
   const void* k;
   const void* v;
   void* out;
+  float* lse;  // each row's log-sum-exp (natural log), or NULL: [B, H, Lq], or [H, total_q] with cu_q
   int B, Lq, Lk, H;
-  long long qs[3], ks[3], vs[3];  // element strides: batch, token, head (dim stride 1)
+  int Hk, G;                       // KV heads, and query heads per KV head (H / Hk)
+  long long qs[3], ks[3], vs[3];   // element strides: batch, token, head (dim stride 1)
+  const int* cu_q;                 // varlen: sequence b's queries are tokens [cu_q[b], cu_q[b+1]), or NULL
+  const int* cu_k;                 // and its keys [cu_k[b], cu_k[b+1]); Lq/Lk are then the largest lengths
+  long long total_q, total_k;      // varlen: tokens of q and of k/v (lse is [H, total_q])
   float c;                         // softmax_scale * log2(e)
   int causal;
 };
+
+// A CTA's sequence of a prefill launch: its lengths, where its tokens start
+// and where its output rows and log-sum-exps go.
+struct FlashSeq {
+  int Lq, Lk;          // this sequence's lengths
+  long long tq0, tk0;  // first query / key token (varlen), else 0
+  long long obase;     // output element of (row 0, head 0)
+  long long lbase;     // lse index of row 0 of head h
+};
+
+template <typename P>
+__device__ __forceinline__ FlashSeq flash_seq(const P& p, int b, int h, int E) {
+  FlashSeq s;
+  if (p.cu_q) {
+    s.tq0 = __ldg(p.cu_q + b);
+    s.tk0 = __ldg(p.cu_k + b);
+    s.Lq = __ldg(p.cu_q + b + 1) - (int)s.tq0;
+    s.Lk = __ldg(p.cu_k + b + 1) - (int)s.tk0;
+    s.obase = s.tq0 * p.H * E;
+    s.lbase = (long long)h * p.total_q + s.tq0;
+  } else {
+    s.tq0 = s.tk0 = 0;
+    s.Lq = p.Lq;
+    s.Lk = p.Lk;
+    s.obase = (long long)b * p.Lq * p.H * E;
+    s.lbase = ((long long)b * p.H + h) * p.Lq;
+  }
+  return s;
+}
+
+// log-sum-exp in natural-log units of a row with running max m and sum l
+// (log2 units)
+__device__ __forceinline__ float flash_lse(float m, float l) {
+  return l > 0.f ? (m + log2f(l)) * 0.69314718055994531f : -INFINITY;
+}
 
 // The (query block, head, batch) of a CTA of a 1-D prefill grid of
 // nblk * heads * batch CTAs (launched in index order). Causal grids run in
@@ -71,21 +111,25 @@ __global__ void __launch_bounds__(128) flash_generic_kernel(const __grid_constan
   int blk, h, b;
   flash_block_of((int)blockIdx.x, (p.Lq + BQ - 1) / BQ, p.H, p.causal != 0, &blk, &h, &b);
   const int q0 = blk * BQ;
-  const T* qg = static_cast<const T*>(p.q) + b * p.qs[0] + h * p.qs[2];
-  const T* kg = static_cast<const T*>(p.k) + b * p.ks[0] + h * p.ks[2];
-  const T* vg = static_cast<const T*>(p.v) + b * p.vs[0] + h * p.vs[2];
-  T* og = static_cast<T*>(p.out) + ((long long)b * p.Lq * p.H + h) * E;  // contiguous [B, Lq, H, E]
+  const FlashSeq sq = flash_seq(p, b, h, E);
+  const int Lq = sq.Lq, Lk = sq.Lk;
+  if (q0 >= Lq) return;  // (varlen: past this sequence's rows; uniform per CTA)
+  const int kh = h / p.G;  // its KV head
+  const T* qg = static_cast<const T*>(p.q) + (p.cu_q ? sq.tq0 * p.qs[1] : b * p.qs[0]) + h * p.qs[2];
+  const T* kg = static_cast<const T*>(p.k) + (p.cu_q ? sq.tk0 * p.ks[1] : b * p.ks[0]) + kh * p.ks[2];
+  const T* vg = static_cast<const T*>(p.v) + (p.cu_q ? sq.tk0 * p.vs[1] : b * p.vs[0]) + kh * p.vs[2];
+  T* og = static_cast<T*>(p.out) + sq.obase + (long long)h * E;  // contiguous [tokens, H, E]
   const long long ostride = (long long)p.H * E;
-  const int diag = p.Lk - p.Lq;
+  const int diag = Lk - Lq;
 
   // Q rows of this CTA (rows past Lq read as 0)
   for (int x = threadIdx.x; x < BQ * E; x += blockDim.x) {
     const int r = x / E, d = x - r * E;
     const int qi = q0 + r;
-    sQ[x] = qi < p.Lq ? to_f32(qg[(long long)qi * p.qs[1] + d]) : 0.f;
+    sQ[x] = qi < Lq ? to_f32(qg[(long long)qi * p.qs[1] + d]) : 0.f;
   }
 
-  const int kend = p.causal ? min(p.Lk, q0 + BQ + diag) : p.Lk;  // keys [0, kend) can be visible
+  const int kend = p.causal ? min(Lk, q0 + BQ + diag) : Lk;  // keys [0, kend) can be visible
   float m[RW], lp[RW], o[RW][DPL];
 #pragma unroll
   for (int r = 0; r < RW; ++r) {
@@ -103,7 +147,7 @@ __global__ void __launch_bounds__(128) flash_generic_kernel(const __grid_constan
       const int j = x / E, d = x - j * E;
       const int kj = k0 + j;
       float kv = 0.f, vv = 0.f;
-      if (kj < p.Lk) {
+      if (kj < Lk) {
         kv = to_f32(kg[(long long)kj * p.ks[1] + d]);
         vv = to_f32(vg[(long long)kj * p.vs[1] + d]);
       }
@@ -143,7 +187,7 @@ __global__ void __launch_bounds__(128) flash_generic_kernel(const __grid_constan
 #pragma unroll
     for (int r = 0; r < RW; ++r) {
       const int qi = wr0 + r;
-      const int lim = p.causal ? min(p.Lk - 1, qi + diag) : p.Lk - 1;  // last visible key
+      const int lim = p.causal ? min(Lk - 1, qi + diag) : Lk - 1;  // last visible key
       const int j0 = k0 + lane, j1 = k0 + lane + 32;
       const float x0 = (j0 <= lim) ? s0[r] * p.c : -INFINITY;
       const float x1 = (j1 <= lim) ? s1[r] * p.c : -INFINITY;
@@ -189,10 +233,11 @@ __global__ void __launch_bounds__(128) flash_generic_kernel(const __grid_constan
   for (int r = 0; r < RW; ++r) {
     const int qi = wr0 + r;
     const float l = warp_sum(lp[r]);
-    if (qi < p.Lq) {
+    if (qi < Lq) {
       const float inv = l > 0.f ? 1.f / l : 0.f;
 #pragma unroll
       for (int c = 0; c < DPL; ++c) og[qi * ostride + lane * DPL + c] = from_f32<T>(l > 0.f ? o[r][c] * inv : 0.f);
+      if (p.lse && lane == 0) p.lse[sq.lbase + qi] = flash_lse(m[r], l);
     }
   }
 }

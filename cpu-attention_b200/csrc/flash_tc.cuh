@@ -38,10 +38,15 @@
 namespace ca {
 
 struct FlashTcArgs {
-  CUtensorMap tq, tk, tv;  // 4-D maps {E, tokens, heads, batch}, bf16
-  void* out;               // [B, Lq, H, E] contiguous
-  int B, Lq, Lk, H;
-  float c;  // softmax_scale * log2(e)
+  CUtensorMap tq, tk, tv;  // 4-D maps {E, tokens, heads, batch}, bf16 (varlen: batch 1)
+  void* out;               // [B, Lq, H, E] contiguous (varlen: [total_q, H, E])
+  float* lse;              // [B, H, Lq] (varlen: [H, total_q]) or NULL
+  long long total_q;       // varlen: query tokens (the lse row length)
+  const int* cu_q;         // varlen sequence starts (see FlashParams), or NULL
+  const int* cu_k;
+  int B, Lq, Lk, H;        // varlen: Lq, Lk are the largest lengths
+  int G;                   // query heads per KV head
+  float c;                 // softmax_scale * log2(e)
   int causal;
   int* status;
 };
@@ -161,7 +166,12 @@ __global__ void __launch_bounds__(384, 1) flash_tc_kernel(const __grid_constant_
   int blk, h, b;
   flash_block_of((int)blockIdx.x, nblk, a.H, CAUSAL, &blk, &h, &b);
   const int q0 = blk * C::ROWS;
-  const int nt0 = tc_tiles(q0, a.Lq, a.Lk, CAUSAL), nt1 = tc_tiles(q0 + C::BM, a.Lq, a.Lk, CAUSAL);
+  const FlashSeq sq = flash_seq(a, b, h, E);
+  const int Lq = sq.Lq, Lk = sq.Lk;
+  const int kh = h / a.G;                    // the KV head of query head h
+  const int tb = a.cu_q ? 0 : b;             // TMA batch coordinate
+  const int tq = (int)sq.tq0, tk = (int)sq.tk0;  // TMA token offsets (varlen)
+  const int nt0 = tc_tiles(q0, Lq, Lk, CAUSAL), nt1 = tc_tiles(q0 + C::BM, Lq, Lk, CAUSAL);
   const int nt = max(nt0, nt1);
 
   if (threadIdx.x == 0) {
@@ -199,8 +209,8 @@ __global__ void __launch_bounds__(384, 1) flash_tc_kernel(const __grid_constant_
       for (int x = 0; x < nq; ++x)
 #pragma unroll
         for (int ch = 0; ch < C::NCH; ++ch)
-          tc::tma_load_4d(sQ + x * C::TILE_BYTES + ch * C::CH_BYTES, &a.tq, ch * C::CHUNK, q0 + x * C::BM, h, b,
-                          &bars->q);
+          tc::tma_load_4d(sQ + x * C::TILE_BYTES + ch * C::CH_BYTES, &a.tq, ch * C::CHUNK, tq + q0 + x * C::BM, h,
+                          tb, &bars->q);
       // K runs ahead of V: K_j is needed by S(j), V_j only by the later PV(j)
       int jv = 0;
       for (int j = 0; j < nt; ++j) {
@@ -209,8 +219,8 @@ __global__ void __launch_bounds__(384, 1) flash_tc_kernel(const __grid_constant_
         mbar_arrive_expect_tx(&bars->kf[ks], C::TILE_BYTES);
 #pragma unroll
         for (int ch = 0; ch < C::NCH; ++ch)
-          tc::tma_load_4d(sK + ks * C::TILE_BYTES + ch * C::CH_BYTES, &a.tk, ch * C::CHUNK, j * C::BN, h, b,
-                          &bars->kf[ks]);
+          tc::tma_load_4d(sK + ks * C::TILE_BYTES + ch * C::CH_BYTES, &a.tk, ch * C::CHUNK, tk + j * C::BN, kh,
+                          tb, &bars->kf[ks]);
         // the V tiles whose slot is free by now
         for (; jv <= j; ++jv) {
           const int vs = jv % C::VST;
@@ -218,8 +228,8 @@ __global__ void __launch_bounds__(384, 1) flash_tc_kernel(const __grid_constant_
           mbar_arrive_expect_tx(&bars->vf[vs], C::TILE_BYTES);
 #pragma unroll
           for (int ch = 0; ch < C::NCH; ++ch)
-            tc::tma_load_4d(sV + vs * C::TILE_BYTES + ch * C::CH_BYTES, &a.tv, ch * C::CHUNK, jv * C::BN, h, b,
-                            &bars->vf[vs]);
+            tc::tma_load_4d(sV + vs * C::TILE_BYTES + ch * C::CH_BYTES, &a.tv, ch * C::CHUNK, tk + jv * C::BN, kh,
+                            tb, &bars->vf[vs]);
         }
       }
       for (; jv < nt && !*abort; ++jv) {
@@ -228,8 +238,8 @@ __global__ void __launch_bounds__(384, 1) flash_tc_kernel(const __grid_constant_
         mbar_arrive_expect_tx(&bars->vf[vs], C::TILE_BYTES);
 #pragma unroll
         for (int ch = 0; ch < C::NCH; ++ch)
-          tc::tma_load_4d(sV + vs * C::TILE_BYTES + ch * C::CH_BYTES, &a.tv, ch * C::CHUNK, jv * C::BN, h, b,
-                          &bars->vf[vs]);
+          tc::tma_load_4d(sV + vs * C::TILE_BYTES + ch * C::CH_BYTES, &a.tv, ch * C::CHUNK, tk + jv * C::BN, kh,
+                          tb, &bars->vf[vs]);
       }
       // leave only after every load this CTA issued has landed
       for (int j = max(0, nt - C::KST); j < nt; ++j)
@@ -298,7 +308,7 @@ __global__ void __launch_bounds__(384, 1) flash_tc_kernel(const __grid_constant_
     const uint32_t lrow = tmem + ((uint32_t)(grp * 32) << 16);
     const uint32_t tS = lrow + C::T_S(x), tO = lrow + C::T_O(x);
     const int qi = q0 + x * C::BM + r;
-    const int lim = CAUSAL ? min(a.Lk - 1, qi + a.Lk - a.Lq) : a.Lk - 1;  // last key this row sees
+    const int lim = CAUSAL ? min(Lk - 1, qi + Lk - Lq) : Lk - 1;  // last key this row sees
     const int ntr = (x ? nt1 : nt0);
     // masked scores get a value that scale * value maps to -inf
     const float sent = a.c >= 0.f ? -INFINITY : INFINITY;
@@ -412,8 +422,8 @@ __global__ void __launch_bounds__(384, 1) flash_tc_kernel(const __grid_constant_
       mbar_arrive(&bars->p[x]);
     }
     // ---- epilogue: out = O / l (0 for a row that saw no key)
-    if (q0 + x * C::BM < a.Lq) {
-      __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(a.out) + (((long long)b * a.Lq + qi) * a.H + h) * E;
+    if (q0 + x * C::BM < Lq) {
+      __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(a.out) + sq.obase + ((long long)qi * a.H + h) * E;
       const bool have =
           ok && ntr > 0 && __all_sync(0xffffffffu, tc_wait(&bars->pv[x], (ntr - 1) & 1, abort, a.status));
       if (have) tc::fence_after_sync();
@@ -425,7 +435,7 @@ __global__ void __launch_bounds__(384, 1) flash_tc_kernel(const __grid_constant_
           tc::tmem_ld32(tO + c4 * 32, rr);
           tc::tmem_ld_wait();
         }
-        if (qi < a.Lq) {
+        if (qi < Lq) {
           uint4 w[4];
           uint32_t* wp = reinterpret_cast<uint32_t*>(w);
 #pragma unroll
@@ -439,6 +449,7 @@ __global__ void __launch_bounds__(384, 1) flash_tc_kernel(const __grid_constant_
           for (int i = 0; i < 4; ++i) dst[i] = w[i];
         }
       }
+      if (a.lse && qi < Lq) a.lse[sq.lbase + qi] = have ? flash_lse(m, l) : -INFINITY;
     }
   }
   tc::fence_before_sync();
@@ -497,15 +508,27 @@ template <int E>
 int flash_tc_launch(const FlashParams& p, int* status, cudaStream_t stream, std::string* err) {
   using C = TcCfg<E>;
   FlashTcArgs a;
-  if (!make_tile_map<E>(&a.tq, p.q, p.Lq, p.H, p.B, p.qs) || !make_tile_map<E>(&a.tk, p.k, p.Lk, p.H, p.B, p.ks) ||
-      !make_tile_map<E>(&a.tv, p.v, p.Lk, p.H, p.B, p.vs))
+  // varlen: one batch of total_q / total_k tokens; the kernel offsets each
+  // sequence's token coordinates
+  const bool var = p.cu_q != nullptr;
+  const long long nq = var ? p.total_q : p.Lq, nk = var ? p.total_k : p.Lk, nb = var ? 1 : p.B;
+  const long long qs[3] = {var ? nq * p.qs[1] : p.qs[0], p.qs[1], p.qs[2]};
+  const long long ks[3] = {var ? nk * p.ks[1] : p.ks[0], p.ks[1], p.ks[2]};
+  const long long vs[3] = {var ? nk * p.vs[1] : p.vs[0], p.vs[1], p.vs[2]};
+  if (!make_tile_map<E>(&a.tq, p.q, nq, p.H, nb, qs) || !make_tile_map<E>(&a.tk, p.k, nk, p.Hk, nb, ks) ||
+      !make_tile_map<E>(&a.tv, p.v, nk, p.Hk, nb, vs))
     return CA_EUNSUPPORTED;
   if (reinterpret_cast<uintptr_t>(p.out) & 15) return CA_EUNSUPPORTED;
   a.out = p.out;
+  a.lse = p.lse;
+  a.total_q = p.total_q;
+  a.cu_q = p.cu_q;
+  a.cu_k = p.cu_k;
   a.B = p.B;
   a.Lq = p.Lq;
   a.Lk = p.Lk;
   a.H = p.H;
+  a.G = p.G;
   a.c = p.c;
   a.causal = p.causal;
   a.status = status;

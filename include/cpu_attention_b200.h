@@ -130,6 +130,29 @@ CA_API int ca_decode_append(const void* q, int64_t q_stride, void* k_cache,
               int64_t head_dim, int64_t page, int dtype, float softmax_scale,
               void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- the general decode entry: grouped heads, log-sum-exp -----------------
+ * ca_decode and ca_decode_append in one entry, with two capabilities the
+ * reference declines (`flash_attn_interface.py:87-96`, `:144-145`):
+ * kv_heads: the heads of the caches and of k_new/v_new; heads % kv_heads == 0
+ *   and query head h attends KV head h / (heads / kv_heads) (GQA; MQA at
+ *   kv_heads = 1). kv_heads == heads is ca_decode.
+ * lse: NULL, or float32 [batch, heads]: each row's log-sum-exp,
+ *   ln(sum_t exp(scale * q . k_t)), -inf for a row that sees no key
+ *   (flash-attn's softmax_lse).
+ * n_new: 0 (k_new/v_new NULL: no new tokens), 1 (stored at slots[i], or
+ *   appended at lens[i] when slots is NULL) or more (appended at lens[i],
+ *   kv_token_stride elements apart; slots NULL).
+ * The workspace is ca_decode_workspace_bytes(batch, heads, ...) long.
+ */
+CA_API int ca_decode_ex(const void* q, int64_t q_stride, void* k_cache,
+              void* v_cache, int64_t num_blocks, const void* k_new,
+              const void* v_new, int64_t kv_stride, int64_t kv_token_stride,
+              int64_t n_new, const int64_t* slots, const int32_t* lens,
+              const int32_t* page_table, int64_t table_width, void* out,
+              float* lse, int64_t batch, int64_t heads, int64_t kv_heads,
+              int64_t head_dim, int64_t page, int dtype, float softmax_scale,
+              void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- paged decode without allocation -----------------------------------
  * No counterpart in the reference: an addition for callers that cannot
  * allocate device memory (an engine that reserves all GPU memory up front and
@@ -173,6 +196,32 @@ CA_API int ca_flash(const void* q, const void* k, const void* v, void* out,
              int64_t batch, int64_t seq_q, int64_t seq_k, int64_t heads,
              int64_t head_dim, const int64_t q_strides[3],
              const int64_t k_strides[3], const int64_t v_strides[3],
+             float softmax_scale, int causal, int dtype, int32_t* status,
+             void* stream);
+
+/* ---- the general prefill entry: grouped heads, log-sum-exp, varlen -------
+ * ca_flash with three capabilities the reference declines
+ * (`flash_attn_interface.py:144-145`, `:215-218`):
+ * kv_heads: k/v's heads; heads % kv_heads == 0 and query head h attends KV
+ *   head h / (heads / kv_heads) (GQA; MQA at kv_heads = 1).
+ * lse: NULL, or float32 rows of log-sum-exp, ln(sum_j exp(scale * q . k_j)),
+ *   -inf for a row that sees no key: [batch, heads, seq_q] (dense) or
+ *   [heads, total_q] (varlen) -- flash-attn's softmax_lse.
+ * cu_seqlens_q / cu_seqlens_k: NULL (dense), or device int32 [batch + 1]
+ *   (varlen, flash_attn_varlen_func): sequence b's queries are tokens
+ *   [cu_seqlens_q[b], cu_seqlens_q[b + 1]) of q [total_q, heads, head_dim] and
+ *   its keys tokens [cu_seqlens_k[b], cu_seqlens_k[b + 1]) of k/v
+ *   [total_k, kv_heads, head_dim]; seq_q / seq_k are then the largest
+ *   sequence lengths (no sequence may exceed them), the strides' batch entry
+ *   is ignored, out is [total_q, heads, head_dim] and causal masks per
+ *   sequence (bottom-right). total_q / total_k are ignored when dense.
+ */
+CA_API int ca_flash_ex(const void* q, const void* k, const void* v, void* out,
+             float* lse, int64_t batch, int64_t seq_q, int64_t seq_k,
+             int64_t heads, int64_t kv_heads, int64_t head_dim,
+             const int64_t q_strides[3], const int64_t k_strides[3],
+             const int64_t v_strides[3], const int32_t* cu_seqlens_q,
+             const int32_t* cu_seqlens_k, int64_t total_q, int64_t total_k,
              float softmax_scale, int causal, int dtype, int32_t* status,
              void* stream);
 

@@ -40,6 +40,24 @@ def attention(q, k, v, scale, causal=False):
     return np.ascontiguousarray(np.matmul(p, v).transpose(0, 2, 1, 3))
 
 
+def logsumexp(q, k, v, scale, causal=False):
+    """The softmax log-sum-exp of every row, float64 [b, h, sq]: ln of the sum
+    over the keys row i sees of exp(scale * q_i . k_j), -inf for a row that sees
+    none (flash-attn's softmax_lse; the reference computes no such output, so
+    this follows the definition with the mask of `attention`). v is unused."""
+    del v
+    q, k = (as_f64(x).transpose(0, 2, 1, 3) for x in (q, k))
+    w = np.matmul(q, k.transpose(0, 1, 3, 2)) * scale
+    sq, sk = q.shape[2], k.shape[2]
+    if causal:
+        mask = np.arange(sk)[None, :] > np.arange(sq)[:, None] + sk - sq
+        w = np.where(mask, -np.inf, w)
+    mx = w.max(axis=-1, initial=-np.inf)
+    safe = np.where(np.isfinite(mx), mx, 0.0)
+    with np.errstate(divide="ignore"):
+        return np.log(np.exp(w - safe[..., None]).sum(axis=-1)) + safe
+
+
 def bf16_round(x):
     """float64 -> nearest bf16 (ties to even), back as float64."""
     f = np.asarray(x, dtype=np.float32)

@@ -96,3 +96,97 @@ def decode_cases():
         scale = r.choice([1.0, 0.5]) * d ** -0.5
         out.append((f"d_fuzz_{seed}", lens, h, d, page, dtype, seed, scale))
     return out
+
+
+# ---- grouped heads (GQA/MQA) and packed sequences (varlen) -----------------
+# The reference declines both; its float64 oracle is MHA over padded batches,
+# so their golden outputs come from it with K/V heads repeated to the query
+# heads (query head h reads KV head h // (h_q // h_kv)) and from one call per
+# sequence (tests/golden/make_golden.py).
+GQA_HEADS = [(4, 2), (6, 2), (8, 2), (10, 2), (16, 2), (8, 1)]  # groups 2, 3, 4, 5, 8 and MQA
+GQA_MQA32 = (32, 1)  # a group of 32: four items of eight rows per KV head
+
+
+def expand_kv(x, heads):
+    """[..., h_kv, d] -> [..., heads, d]: each KV head repeated for its group."""
+    return x.repeat_interleave(heads // x.shape[-2], dim=-2)
+
+
+def gqa_flash_inputs(b, sq, sk, h, hk, d, dtype, seed):
+    """q [b, sq, h, d], k/v [b, sk, hk, d], drawn in that order."""
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(b, sq, h, d, generator=g).to(dtype),
+            torch.randn(b, sk, hk, d, generator=g).to(dtype),
+            torch.randn(b, sk, hk, d, generator=g).to(dtype))
+
+
+def gqa_flash_cases():
+    """(name, b, sq, sk, h, hk, d, dtype, causal, seed) of the golden GQA prefill set."""
+    out = []
+    for dtype in DTYPES:
+        dn = "bf16" if dtype == torch.bfloat16 else "fp32"
+        for n, (h, hk) in enumerate(GQA_HEADS[:4] + [GQA_HEADS[5]]):
+            d = (64, 128, 32, 32, 64)[n]
+            for causal in (True, False):
+                for sq, sk in ((17, 17), (40, 150)):
+                    out.append((f"g_{dn}_h{h}k{hk}_d{d}_{sq}x{sk}_c{int(causal)}", 1, sq, sk, h, hk, d, dtype,
+                                causal, 7 * n + sq))
+    return out
+
+
+def gqa_stage_inputs(lens, h, hk, d, page, dtype, seed):
+    """stage_inputs with q of h heads and K/V of hk heads."""
+    g = torch.Generator().manual_seed(seed)
+    npages = [-(-n // page) for n in lens]
+    total = sum(npages) + 1
+    order = torch.randperm(total, generator=g).to(torch.int32)
+    bt = torch.full((len(lens), max(npages) + 1), int(order[-1]), dtype=torch.int32)
+    q = torch.randn(len(lens), 1, h, d, generator=g).to(dtype)
+    ks, vs, start = [], [], 0
+    for i, n in enumerate(lens):
+        bt[i, :npages[i]] = order[start:start + npages[i]]
+        start += npages[i]
+        k, v = (torch.randn(1, n, hk, d, generator=g).to(dtype) for _ in range(2))
+        ks.append(k)
+        vs.append(v)
+    return q, bt, total, ks, vs
+
+
+def gqa_decode_cases():
+    """(name, lens, h, hk, d, page, dtype, seed, scale) of the golden GQA decode set."""
+    out = []
+    for dtype in DTYPES:
+        dn = "bf16" if dtype == torch.bfloat16 else "fp32"
+        for n, (h, hk) in enumerate(GQA_HEADS + [GQA_MQA32]):
+            for page in (16, 32):
+                d = (128, 64, 32)[(n + page // 16) % 3] if h <= 10 else 32
+                out.append((f"gd_{dn}_h{h}k{hk}_d{d}_p{page}", [0, 1, page, page + 1, 300, 2047], h, hk, d, page,
+                            dtype, 100 * n + page, None))
+    return out
+
+
+def varlen_inputs(lq, lk, h, hk, d, dtype, seed):
+    """Packed q [sum(lq), h, d], k/v [sum(lk), hk, d] and int32 offsets."""
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(sum(lq), h, d, generator=g).to(dtype)
+    k = torch.randn(sum(lk), hk, d, generator=g).to(dtype)
+    v = torch.randn(sum(lk), hk, d, generator=g).to(dtype)
+    cq = torch.tensor([0] + list(torch.tensor(lq).cumsum(0)), dtype=torch.int32)
+    ck = torch.tensor([0] + list(torch.tensor(lk).cumsum(0)), dtype=torch.int32)
+    return q, k, v, cq, ck
+
+
+def varlen_cases():
+    """(name, lq, lk, h, hk, d, dtype, causal, seed): ragged batches with empty,
+    single-token, tile-edge and unequal q/k lengths."""
+    shapes = [([5, 1, 130, 64], [5, 7, 130, 200]), ([100, 0, 17], [100, 33, 17]), ([128, 129], [128, 260]),
+              ([1, 260], [300, 260])]
+    out = []
+    for dtype in DTYPES:
+        dn = "bf16" if dtype == torch.bfloat16 else "fp32"
+        for n, (lq, lk) in enumerate(shapes):
+            h, hk = ((2, 2), (4, 2), (3, 3), (2, 1))[n]
+            d = (64, 128, 32, 32)[n]
+            for causal in (True, False):
+                out.append((f"v_{dn}_{n}_c{int(causal)}", lq, lk, h, hk, d, dtype, causal, 11 * n + 1))
+    return out

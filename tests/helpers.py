@@ -27,17 +27,21 @@ def append_slots(bt, lens_before, n, page):
     return out
 
 
-def stage_cache(lens, h, d, page, dtype, seed, store, device="cpu"):
+def stage_cache(lens, h, d, page, dtype, seed, store, device="cpu", gqa=None):
     """The reference's ``stage`` (test_kvcache.py:118-141): caches holding
     ``lens[i]`` random tokens per sequence, everything else NaN (unused slots and
     pages, and the page-table padding, which points at a poisoned page). Tokens
     are written with ``store(key, value, kc, vc, slots)`` in two halves per
-    sequence, as the reference stages through two appends.
+    sequence, as the reference stages through two appends. ``gqa``: the number
+    of KV heads (``cases.gqa_stage_inputs``), else every head has its own.
 
     Returns (q [B,1,h,d], kc, vc, bt, ks, vs) on ``device``.
     """
-    q, bt, total, ks, vs = cases.stage_inputs(lens, h, d, page, dtype, seed)
-    kc = torch.full((total, h, page, d), float("nan"), dtype=dtype, device=device)
+    if gqa is None:
+        q, bt, total, ks, vs = cases.stage_inputs(lens, h, d, page, dtype, seed)
+    else:
+        q, bt, total, ks, vs = cases.gqa_stage_inputs(lens, h, gqa, d, page, dtype, seed)
+    kc = torch.full((total, gqa or h, page, d), float("nan"), dtype=dtype, device=device)
     vc = kc.clone()
     for i, n in enumerate(lens):
         for a, z in ((0, n // 2), (n // 2, n)):

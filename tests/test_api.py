@@ -24,11 +24,13 @@ def paged():
 
 
 @pytest.mark.parametrize("kwargs", [
-    dict(window_size=(8, 0)), dict(softcap=30.0), dict(return_softmax_lse=True),
-    dict(attention_chunk=64), dict(rotary_cos=torch.ones(1)), dict(qv=torch.ones(1)),
-    dict(alibi_slopes=torch.ones(4)),
+    dict(window_size=(8, 0)), dict(softcap=30.0), dict(attention_chunk=64), dict(rotary_cos=torch.ones(1)),
+    dict(qv=torch.ones(1)), dict(alibi_slopes=torch.ones(4)), dict(window_size=[4, 4]),
+    dict(cu_seqlens_q=torch.ones(1)), dict(k_descale=torch.ones(1)),
 ])
 def test_kvcache_unsupported_options(kwargs):
+    """The reference's list (`tests/test_api.py:15-24`) minus return_softmax_lse,
+    which this build computes."""
     q, kc, vc, bt = paged()
     with pytest.raises(NotImplementedError):
         C.flash_attn_with_kvcache(q, kc, vc, cache_seqlens=4, page_table=bt, **kwargs)
@@ -70,14 +72,25 @@ def test_kvcache_cpu_tensors_are_refused():
 
 
 @pytest.mark.parametrize("kv_heads", [2, 1])
-def test_gqa_mqa_not_supported_yet(kv_heads):
+def test_gqa_mqa_accepted(kv_heads):
+    """Grouped heads are no longer refused (the reference raises
+    NotImplementedError, `tests/test_api.py:52-59`): a call with nheads_k
+    dividing nheads gets as far as the device check, and one whose nheads_k
+    does not divide nheads is a ValueError."""
     q, kc, vc, bt = paged()
     kc = torch.zeros(4, kv_heads, 16, 64)
-    with pytest.raises(NotImplementedError):
+    with pytest.raises(ValueError, match="CUDA"):
         C.flash_attn_with_kvcache(q, kc, kc.clone(), cache_seqlens=4, page_table=bt)
     k = torch.randn(2, 8, kv_heads, 64)
-    with pytest.raises(NotImplementedError):
+    with pytest.raises(ValueError, match="CUDA"):
         C.flash_attn_func(torch.randn(2, 8, 4, 64), k, k)
+    with pytest.raises(ValueError):
+        C.flash_attn_func(torch.randn(2, 8, 3, 64), k, k)
+    with pytest.raises(ValueError):
+        C.flash_attn_with_kvcache(q[:, :, :3], kc, kc.clone(), cache_seqlens=4, page_table=bt)
+    kn = torch.randn(2, 1, 4, 64)  # new tokens must carry nheads_k heads
+    with pytest.raises(ValueError, match="k/v"):
+        C.flash_attn_with_kvcache(q, kc, kc.clone(), k=kn, v=kn, cache_seqlens=4, page_table=bt)
 
 
 @pytest.mark.parametrize("bad", ["dtype", "heads", "slots_dtype", "slots_len", "past_end"])
@@ -114,8 +127,37 @@ def test_flash_bad_arguments(bad):
         C.flash_attn_func(q, k, k)
 
 
-@pytest.mark.parametrize("fn", [C.flash_attn_varlen_func, C.flash_attn_qkvpacked_func,
-                                C.flash_attn_kvpacked_func,
+@pytest.mark.parametrize("bad", ["dims", "heads", "cu_dtype", "cu_len", "cu_order", "cu_past_end", "max"])
+def test_varlen_bad_arguments(bad):
+    q, k = torch.randn(10, 4, 64), torch.randn(12, 2, 64)
+    cq, ck = torch.tensor([0, 4, 10], dtype=torch.int32), torch.tensor([0, 5, 12], dtype=torch.int32)
+    mq, mk = 6, 7
+    if bad == "dims":
+        q = q[None]
+    elif bad == "heads":
+        k = torch.randn(12, 3, 64)
+    elif bad == "cu_dtype":
+        cq = cq.long()
+    elif bad == "cu_len":
+        ck = ck[:2]
+    elif bad == "cu_order":
+        cq = torch.tensor([0, 6, 4], dtype=torch.int32)
+    elif bad == "cu_past_end":
+        ck = torch.tensor([0, 5, 13], dtype=torch.int32)
+    elif bad == "max":
+        mq = 5  # the second sequence has 6 queries
+    with pytest.raises(ValueError):
+        C.flash_attn_varlen_func(q, k, k, cq, ck, mq, mk)
+
+
+def test_varlen_valid_call_on_cpu_is_refused():
+    q, k = torch.randn(10, 4, 64), torch.randn(12, 2, 64)
+    cq, ck = torch.tensor([0, 4, 10], dtype=torch.int32), torch.tensor([0, 5, 12], dtype=torch.int32)
+    with pytest.raises(ValueError, match="CUDA"):
+        C.flash_attn_varlen_func(q, k, k, cq, ck, 6, 7, causal=True)
+
+
+@pytest.mark.parametrize("fn", [C.flash_attn_qkvpacked_func, C.flash_attn_kvpacked_func,
                                 C.flash_attn_varlen_qkvpacked_func,
                                 C.flash_attn_varlen_kvpacked_func])
 def test_not_ported(fn):

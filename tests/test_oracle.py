@@ -180,3 +180,77 @@ def test_exp2_polynomials_error_bounds():
         w = 1.0 / (1.0 + 2.0 ** -g)
         assert abs(out[0, 0, 1].item() - w) < 1e-6
         assert abs(out[0, 0, 2].item() - (1 - w)) < 1e-6
+
+
+# ------------------------------------------- grouped heads, varlen, log-sum-exp --
+def test_extension_inputs_match_golden_digests():
+    g = golden("ext")
+    for name, b, sq, sk, h, hk, d, dtype, causal, seed in cases.gqa_flash_cases():
+        assert str(g[name + "__digest"]) == cases.digest(*cases.gqa_flash_inputs(b, sq, sk, h, hk, d, dtype,
+                                                                                 seed)), name
+    for name, lens, h, hk, d, page, dtype, seed, scale in cases.gqa_decode_cases():
+        q, bt, total, ks, vs = cases.gqa_stage_inputs(lens, h, hk, d, page, dtype, seed)
+        assert str(g[name + "__digest"]) == cases.digest(q, bt, *ks, *vs), name
+    for name, lq, lk, h, hk, d, dtype, causal, seed in cases.varlen_cases():
+        assert str(g[name + "__digest"]) == cases.digest(*cases.varlen_inputs(lq, lk, h, hk, d, dtype, seed)), name
+
+
+def test_f64_oracle_matches_extension_golden():
+    """The float64 restatement, given K/V heads repeated to the query heads and
+    one call per packed sequence, reproduces the reference oracle's outputs
+    (stored as float32)."""
+    g = golden("ext")
+    for name, b, sq, sk, h, hk, d, dtype, causal, seed in cases.gqa_flash_cases():
+        q, k, v = cases.gqa_flash_inputs(b, sq, sk, h, hk, d, dtype, seed)
+        got = F64.attention(q, cases.expand_kv(k, h), cases.expand_kv(v, h), d ** -0.5, causal)
+        np.testing.assert_allclose(got, g[name], rtol=0, atol=5e-7, err_msg=name)
+    for name, lens, h, hk, d, page, dtype, seed, scale in cases.gqa_decode_cases():
+        q, bt, total, ks, vs = cases.gqa_stage_inputs(lens, h, hk, d, page, dtype, seed)
+        got = np.concatenate([F64.attention(q[i:i + 1], cases.expand_kv(ks[i], h), cases.expand_kv(vs[i], h),
+                                            d ** -0.5) for i in range(len(lens))])
+        np.testing.assert_allclose(got, g[name], rtol=0, atol=5e-7, err_msg=name)
+    for name, lq, lk, h, hk, d, dtype, causal, seed in cases.varlen_cases():
+        q, k, v, cq, ck = cases.varlen_inputs(lq, lk, h, hk, d, dtype, seed)
+        rows = []
+        for i in range(len(lq)):
+            qi = q[int(cq[i]):int(cq[i + 1])][None]
+            ki, vi = (cases.expand_kv(x[int(ck[i]):int(ck[i + 1])], h)[None] for x in (k, v))
+            rows.append(F64.attention(qi, ki, vi, d ** -0.5, causal)[0] if ki.shape[1] else
+                        np.zeros(qi.shape[1:]))
+        np.testing.assert_allclose(np.concatenate(rows), g[name], rtol=0, atol=5e-7, err_msg=name)
+
+
+def test_f64_logsumexp_known_answers():
+    g = torch.Generator().manual_seed(3)
+    q, k = torch.randn(1, 4, 2, 16, generator=g), torch.randn(1, 6, 2, 16, generator=g)
+    s = 0.3
+    lse = F64.logsumexp(q, k, None, s, causal=True)
+    logits = torch.einsum("bqhd,bkhd->bhqk", q.double(), k.double()) * s
+    # bottom-right causal, 4 queries over 6 keys: row i sees keys 0 .. i + 2
+    for i in range(4):
+        np.testing.assert_allclose(lse[0, :, i], torch.logsumexp(logits[0, :, i, :i + 3], -1).numpy(), atol=1e-12)
+    # one visible key: the logit itself; no visible key: -inf
+    lse2 = F64.logsumexp(q, k[:, :1], None, s, causal=True)
+    np.testing.assert_allclose(lse2[0, :, 3], logits[0, :, 3, 0].numpy(), atol=1e-12)
+    assert np.all(np.isneginf(lse2[0, :, :3]))
+
+
+@pytest.mark.parametrize("case", cases.gqa_decode_cases()[:4], ids=lambda c: c[0])
+def test_c_oracle_gqa_decode_on_expanded_caches(case):
+    """The C restatement (MHA, as the reference) on caches whose KV heads are
+    repeated to the query heads passes the reference's paged gates against the
+    grouped-head golden outputs: the check the GPU tests rely on."""
+    name, lens, h, hk, d, page, dtype, seed, scale = case
+    q, kc, vc, bt, ks, vs = stage_cache(lens, h, d, page, dtype, seed, _cpu_store_gqa(hk), gqa=hk)
+    out = torch.empty(len(lens), h, d, dtype=dtype)
+    cpu.decode(q[:, 0].contiguous(), cases.expand_kv(kc.transpose(1, 2), h).transpose(1, 2).contiguous(),
+               cases.expand_kv(vc.transpose(1, 2), h).transpose(1, 2).contiguous(),
+               torch.tensor(lens, dtype=torch.int32), bt, out)
+    err, tol = F64.check(out[:, None], golden("ext")[name], _bf(dtype), paged=True)
+    assert err <= tol, err
+
+
+def _cpu_store_gqa(hk):
+    def store(key, value, kc, vc, slots):
+        cpu.store(key.contiguous(), value.contiguous(), kc, vc, slots)
+    return store
