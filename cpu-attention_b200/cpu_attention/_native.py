@@ -234,7 +234,7 @@ def flash(rt, q, k, v, scale, causal, lse=None, cu_q=None, cu_k=None, max_q=None
         sq, sk, tq, tk = int(max_q), int(max_k), q.shape[0], k.shape[0]
         if sq < 1 or sk < 1:
             return None
-        strides = [(0,) + tuple(x.stride()) for x in (q, k, v)]
+        strides = [(0,) + tuple(x.stride()[:2]) for x in (q, k, v)]
         lse_shape = (heads, tq)
     else:
         b, sq = q.shape[0], q.shape[1]
