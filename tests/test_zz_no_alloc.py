@@ -7,8 +7,11 @@ call, while allocating nothing itself.
 Called through the C ABI directly (ctypes), twice in a row, against ca_decode
 on the same inputs, within the tolerance the decode tests use (bf16 max-abs
 2e-2, fp32 1e-4 relative; the two share one kernel, so they normally agree
-exactly). This file is collected last on purpose, and passes alone in a fresh
-process as well as after the other tests.
+exactly), and against the C restatement of the reference's kernel with the
+same tolerance. After the first call (which looks up the scratch array's
+address) the device's free memory does not move across further calls. This
+file is collected last on purpose, and passes alone in a fresh process as well
+as after the other tests.
 """
 
 import ctypes
@@ -17,6 +20,7 @@ import pytest
 import torch
 
 from helpers import north_star_ok
+from oracle import cpu as ORACLE
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -64,14 +68,25 @@ def test_noalloc_matches_decode_twice(dtype, B, H, E, page):
     ref = torch.empty_like(q)
     assert lib.ca_decode(*_args(q, kc, vc, bt, lens, kn, vn, ref), ws.data_ptr(), ws.numel(), stream) == K.OK
     torch.cuda.synchronize()
+    # the C restatement of the reference kernel on host copies (it appends the
+    # new token at lens[i] too)
+    cpu = torch.empty(q.shape, dtype=dtype)
+    ORACLE.decode(q.cpu(), kc.cpu(), vc.cpu(), lens.cpu(), bt.cpu(), cpu, k_new=kn.cpu(), v_new=vn.cpu())
     # the allocation-free one, two calls in a row (the second reuses what the
-    # first left in the shared scratch)
-    for _ in range(2):
-        out = torch.empty_like(q)
+    # first left in the shared scratch); outputs made before the calls, so
+    # that nothing in the loop allocates
+    outs = [torch.empty_like(q) for _ in range(3)]
+    torch.cuda.synchronize()
+    free = []
+    for out in outs:
         assert lib.ca_decode_noalloc(*_args(q, kc, vc, bt, lens, kn, vn, out), stream) == K.OK
         torch.cuda.synchronize()
+        free.append(torch.cuda.mem_get_info()[0])
         err, tol = north_star_ok(out, ref, dtype)
         assert err <= tol, err
+        err, tol = north_star_ok(out, cpu, dtype)
+        assert err <= tol, err
+    assert free[1] == free[0] and free[2] == free[0], free
 
 
 def test_noalloc_rejects_beyond_its_scratch():
