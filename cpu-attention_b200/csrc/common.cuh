@@ -11,6 +11,8 @@
 
 namespace ca {
 
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: the default limit of every bounded device wait
+
 // ---- bf16 words ----------------------------------------------------------
 // A 32-bit word holding two bf16 values (low half = the even dim). Widening a
 // bf16 to fp32 is exact: its bits become the high half of the fp32 word.

@@ -73,7 +73,6 @@ namespace ca {
 
 constexpr int kDecodeMaxPage = 128;               // tokens per page this kernel stages
 constexpr int kKSlotPadBytes = 64;                // K page slot padding: 16 banks
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s per bounded wait (default)
 constexpr int kDecodeMaxWarps = 12;               // streaming warps per CTA (plus a merger, a feeder and the finishers)
 constexpr int kDecodeAhead = 12;                  // published pages a CTA keeps unclaimed
 constexpr int kDecodeFinishers = 2;               // finisher warps (entry f goes to finisher f % 2)
