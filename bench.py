@@ -589,8 +589,8 @@ class ClockSampler:
 # DRAM bytes (read + write) of one launch of the roofline kernel, from one ncu
 # capture of the same workload (the files under profiles/ give the commands).
 TRAFFIC = {
-    "cfg2": (284.9e6, "profiles/decode_kernel_cfg2.md"),
-    "cfg4": (555.6e6, "profiles/flash_tc_kernel_cfg4.md"),
+    "cfg2": (284.4e6, "profiles/decode_kernel_cfg2.md"),
+    "cfg4": (556.8e6, "profiles/flash_tc_kernel_cfg4.md"),
 }
 
 HOST_HIDE_CYCLES = 400_000  # ~0.2 ms of device spin: longer than the host needs to enqueue one step
@@ -789,7 +789,7 @@ def main():
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
 
-    also = [w for w in args.also.split(",") if w and w != args.workload]
+    also = [w for w in args.also.split(",") if w and w not in (args.workload, "none")]
     sampler = ClockSampler(list(range(world))) if rank == 0 else None
     if sampler:
         sampler.start()
