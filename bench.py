@@ -149,9 +149,10 @@ def _pool(lens, page, extra, g):
 class DecodeSpec:
     """The host-side plan of a decode workload: lengths, page table, slots."""
 
-    def __init__(self, name, label, dtype, B, H, E, page, lens_fn, append, engine=False, width=None):
+    def __init__(self, name, label, dtype, B, H, E, page, lens_fn, append, engine=False, width=None, kv_heads=None):
         self.name, self.label, self.dtype = name, label, dtype
         self.B_all, self.H, self.E, self.page, self.append, self.engine = B, H, E, page, append, engine
+        self.Hk = kv_heads or H  # the caches' heads (fewer than H: grouped query heads)
         self.lens_fn, self.width = lens_fn, width
 
     def plan(self, rank, world):
@@ -186,7 +187,7 @@ class DecodeSpec:
             self.attended = [int(n) for n in self.after]
         else:
             self.attended = [int(n) + extra for n in self.lens]
-        self.kv_bytes = sum(self.attended) * self.H * self.E * self.dtype.itemsize * 2
+        self.kv_bytes = sum(self.attended) * self.Hk * self.E * self.dtype.itemsize * 2
         # token slots of the pre-filled cache (contiguous per sequence)
         seq = torch.cat([torch.full((int(n),), i, dtype=torch.int64) for i, n in enumerate(self.lens)]) \
             if self.B else torch.zeros(0, dtype=torch.int64)
@@ -197,7 +198,7 @@ class DecodeSpec:
     def config(self, world):
         lens = [int(n) for n in self.lens]
         c = {"workload": self.label, "global_batch": self.global_batch, "batch_per_gpu": self.B, "heads": self.H,
-             "head_dim": self.E, "page": self.page, "mean_len": round(sum(lens) / max(1, len(lens)), 1),
+             "kv_heads": self.Hk, "head_dim": self.E, "page": self.page, "mean_len": round(sum(lens) / max(1, len(lens)), 1),
              "append": self.append, "num_blocks": self.nblocks, "table_width": int(self.bt.shape[1]),
              "parallelism": f"sequence-shard x{world}", "l2": "flushed (256 MiB write) before each step"}
         if self.engine:
@@ -220,27 +221,27 @@ class Decode:
         s = spec
         self.dtype, self.B, self.H, self.E, self.page = s.dtype, s.B, s.H, s.E, s.page
         self.engine = s.engine
-        self.kc = torch.empty(s.nblocks, s.H, s.page, s.E, dtype=s.dtype, device=dev)
+        self.kc = torch.empty(s.nblocks, s.Hk, s.page, s.E, dtype=s.dtype, device=dev)
         self.vc = torch.empty_like(self.kc)
         self.bt = s.bt.to(dev)
         self.lens = s.lens.to(dev)
         gd = torch.Generator(device=dev).manual_seed(99 + rank)
         for a in range(0, len(s.fill_slots), 65536):
             sl = s.fill_slots[a:a + 65536].to(dev)
-            k = torch.randn(len(sl), s.H, s.E, generator=gd, device=dev, dtype=torch.float32).to(s.dtype)
-            v = torch.randn(len(sl), s.H, s.E, generator=gd, device=dev, dtype=torch.float32).to(s.dtype)
+            k = torch.randn(len(sl), s.Hk, s.E, generator=gd, device=dev, dtype=torch.float32).to(s.dtype)
+            v = torch.randn(len(sl), s.Hk, s.E, generator=gd, device=dev, dtype=torch.float32).to(s.dtype)
             C.reshape_and_cache(k, v, self.kc, self.vc, sl)
         rnd = lambda *shape: torch.randn(*shape, generator=gd, device=dev, dtype=torch.float32).to(s.dtype)  # noqa
         if s.engine:
             self.q = rnd(s.B, s.H, s.E)
-            self.kn, self.vn = rnd(s.B, s.H, s.E), rnd(s.B, s.H, s.E)
+            self.kn, self.vn = rnd(s.B, s.Hk, s.E), rnd(s.B, s.Hk, s.E)
             self.slots = s.slots.to(dev)
             self.after = s.after.to(dev)
             self.out = torch.empty(s.B, s.H, s.E, dtype=s.dtype, device=dev)
         else:
             self.q = rnd(s.B, 1, s.H, s.E)
-            self.kn = rnd(s.B, 1, s.H, s.E) if s.append else None
-            self.vn = rnd(s.B, 1, s.H, s.E) if s.append else None
+            self.kn = rnd(s.B, 1, s.Hk, s.E) if s.append else None
+            self.vn = rnd(s.B, 1, s.Hk, s.E) if s.append else None
         self.attend_lens = torch.tensor(s.attended, dtype=torch.int32, device=dev)
         # engine: store + decode; a one-token append is fused into the decode
         self.launches_per_step = 2 if s.engine else 1
@@ -492,6 +493,20 @@ DECODE = {
     "cfg3e32": lambda: DecodeSpec("cfg3e32", "cfg3e32: cross-attention decode fp32 B=64 H=8 E=32 page32 len=1500 "
                                   "no append", torch.float32, 64, 8, 32, 32, lambda g: torch.full((64,), 1500),
                                   append=False),
+    # grouped query heads (GQA/MQA; the reference declines them): the bf16
+    # cfg2 shape with 4 and 8 query heads per KV head, and one KV head
+    "gqa4": lambda: DecodeSpec("gqa4", "gqa4: flash_attn_with_kvcache bf16 B=32 H=32 Hk=8 E=128 page16 lens~U[17,2047] "
+                               "+1 append", torch.bfloat16, 32, 32, 128, 16,
+                               lambda g: torch.randint(17, 2048, (32,), generator=g), append=True, width=128,
+                               kv_heads=8),
+    "gqa8": lambda: DecodeSpec("gqa8", "gqa8: flash_attn_with_kvcache bf16 B=32 H=64 Hk=8 E=128 page16 lens~U[17,2047] "
+                               "+1 append", torch.bfloat16, 32, 64, 128, 16,
+                               lambda g: torch.randint(17, 2048, (32,), generator=g), append=True, width=128,
+                               kv_heads=8),
+    "mqa": lambda: DecodeSpec("mqa", "mqa: flash_attn_with_kvcache bf16 B=128 H=32 Hk=1 E=128 page16 lens~U[17,2047] "
+                              "+1 append", torch.bfloat16, 128, 32, 128, 16,
+                              lambda g: torch.randint(17, 2048, (128,), generator=g), append=True, width=128,
+                              kv_heads=1),
     "cfg5": lambda: DecodeSpec("cfg5", "cfg5: engine decode bf16 B=256 H=32 E=128 page16 lens~U[1,8191] "
                                "store+decode out=", torch.bfloat16, 256, 32, 128, 16,
                                lambda g: torch.randint(1, 8192, (256,), generator=g), append=False, engine=True),
@@ -723,7 +738,8 @@ def measure(wl, name, args, world, rank, sampler, flush_host):
            "clocks": sampler.window(t_begin, t_end) if sampler else None}
     if with_gather is not None:
         rec["with_gather"] = with_gather
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    grouped = getattr(getattr(wl, "s", None), "Hk", None) not in (None, getattr(wl, "H", None))
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and not grouped:  # the C restatement is MHA only
         threads = physical_cores()
         sec, cunits, n = cpu_baseline(wl, flush_host, threads)
         rec["cpu_baseline"] = {"value": round(cunits / sec / scale, 4), "unit": unit, "cores": threads,
@@ -748,6 +764,10 @@ def run_reference(args):
         spec = DECODE[args.workload]()
         if spec.engine:
             raise SystemExit("the reference arm stages cfg2/cfg3 decode and the prefill configs")
+        if spec.Hk != spec.H:
+            print(json.dumps({"impl": "reference", "unavailable": "the reference declines grouped query heads "
+                              "(its kernel needs as many KV heads as query heads)"}), flush=True)
+            return 0
         wl = HostDecode(spec.plan(0, 1))
     threads = physical_cores()
     flush = HostFlush()
