@@ -60,7 +60,7 @@ int current_device(int* dev) {
 struct DecodePlan {
   int gr;  // query rows per item (1, 2, 4, 8)
   int stages, warps, stage_bytes, kslot_bytes, page_bytes, warp_bytes, smem_bytes, ctas, pages_per_warp, task_cap,
-      ahead, tail_div;
+      ahead, tail_div, run_cap;
 };
 
 constexpr int kDecodeRingTarget = 16384;  // bytes of ring per warp
@@ -83,12 +83,13 @@ int decode_cta_bytes(int gr, long long head_dim) {
     default: return ca::DecodeCta<8>::bytes((int)head_dim);
   }
 }
-int decode_warp_bytes(int gr, int stages, int stage_bytes) {
+int decode_warp_bytes(int gr, int dtype, int stages, int stage_bytes) {
+  const bool mma = ca::decode_uses_mma(dtype == CA_DTYPE_BF16, gr);
   switch (gr) {
-    case 1: return ca::decode_warp_bytes<1>(stages, stage_bytes);
-    case 2: return ca::decode_warp_bytes<2>(stages, stage_bytes);
-    case 4: return ca::decode_warp_bytes<4>(stages, stage_bytes);
-    default: return ca::decode_warp_bytes<8>(stages, stage_bytes);
+    case 1: return ca::decode_warp_bytes<1>(stages, stage_bytes, mma);
+    case 2: return ca::decode_warp_bytes<2>(stages, stage_bytes, mma);
+    case 4: return ca::decode_warp_bytes<4>(stages, stage_bytes, mma);
+    default: return ca::decode_warp_bytes<8>(stages, stage_bytes, mma);
   }
 }
 
@@ -117,14 +118,14 @@ bool decode_plan(long long head_dim, long long page, int dtype, int gr, const De
   const int budget = dev.max_smem_optin - 1024;
   const int cta = decode_cta_bytes(gr, head_dim);
   int stages = std::max(2, std::min(4, kDecodeRingTarget / pl->stage_bytes));
-  auto fits = [&](int s, int warps) { return warps * decode_warp_bytes(gr, s, pl->stage_bytes) + cta <= budget; };
+  auto fits = [&](int s, int warps) { return warps * decode_warp_bytes(gr, dtype, s, pl->stage_bytes) + cta <= budget; };
   while (stages > 2 && !fits(stages, 1)) --stages;
   if (!fits(stages, 1)) return false;
   int warps = ca::kDecodeMaxWarps;
   while (warps > 1 && !fits(stages, warps)) --warps;
   pl->stages = stages;
   pl->warps = warps;
-  pl->warp_bytes = decode_warp_bytes(gr, stages, pl->stage_bytes);
+  pl->warp_bytes = decode_warp_bytes(gr, dtype, stages, pl->stage_bytes);
   pl->smem_bytes = warps * pl->warp_bytes + cta;
   pl->ctas = dev.sms;
   // task unit: 5 pages per streaming warp (measured 1.5% faster than 4 on the
@@ -136,6 +137,10 @@ bool decode_plan(long long head_dim, long long page, int dtype, int gr, const De
   pl->task_cap = (int)std::min<long long>((long long)kTasksPerSm * dev.sms, (slots - 2) / 2);
   if (pl->task_cap < dev.sms) return false;
   pl->ahead = ca::kDecodeAhead;
+  // pages per run: grouped rows stream a task as one run per warp (their
+  // page states are GR times larger to deposit and merge); one row merges
+  // page by page, which finishes the last tasks sooner
+  pl->run_cap = gr >= 2 ? 64 : 1;
   // the last tasks are half the size of the others (a third: +3% and -1% on
   // cfg2 in two sweeps, -1.5% on the E=32 cross-attention case)
   pl->tail_div = 2;
@@ -321,6 +326,7 @@ int decode_impl(const void* q, int64_t q_stride, void* k_cache, void* v_cache, i
   prm.warps = pl.warps;
   prm.pages_per_warp = pl.pages_per_warp;
   prm.ahead = pl.ahead;
+  prm.run_cap = pl.run_cap;
   prm.tail_div = pl.tail_div;
   prm.task_cap = pl.task_cap;
   prm.partial = partial;

@@ -74,7 +74,7 @@ namespace ca {
 constexpr int kDecodeMaxPage = 128;               // tokens per page this kernel stages
 constexpr int kKSlotPadBytes = 64;                // K page slot padding: 16 banks
 constexpr int kDecodeMaxWarps = 12;               // streaming warps per CTA (plus a merger, a feeder and the finishers)
-constexpr int kDecodeAhead = 12;                  // published pages a CTA keeps unclaimed
+constexpr int kDecodeAhead = 3;                   // published, not yet computed pages a CTA keeps per streaming warp
 constexpr int kDecodeFinishers = 2;               // finisher warps (entry f goes to finisher f % 2)
 constexpr int kDecodeBlkRing = 512;               // staged block ids per CTA (a ring over the page stream)
 constexpr int kDecodeBlkTask = 256;               // tasks up to this many pages stage their block ids
@@ -122,7 +122,8 @@ struct DecodeParams {
   int page_bytes;      // bytes of one (block, head) page of K (equally of V)
   int warps;           // streaming warps per CTA (two more warps serve them)
   int pages_per_warp;  // task size U = warps * pages_per_warp (or more)
-  int ahead;           // published pages the feeder keeps unclaimed
+  int run_cap;         // pages per run at most (a task of n pages makes max(min(warps, n), ceil(n / run_cap)) runs)
+  int ahead;           // pages per streaming warp the feeder keeps published but not yet computed
   int tail_div;        // the last tasks are 1 / tail_div the size of the others
   int task_cap;        // split tasks number at most 2 * task_cap
   float* partial;      // [2 * task_cap + 2][GR][E + 2]
@@ -252,6 +253,7 @@ struct QueueEntry {
   int pg0;         // first page of the task
   int n;           // pages of the task
   int start;       // the task's first page in the CTA's page stream
+  int rstart, nr;  // the task's first run in the CTA's run stream, and its runs
   int len;         // attended length of sequence i
   int raw;         // cache_seqlens[i]: the appended tokens sit at [raw, raw + extra)
   int apg0, apg1;  // this task's pages holding appended tokens ([apg0, apg1]; apg0 > apg1: none)
@@ -283,11 +285,28 @@ struct DecodeCta {
   }
 };
 
-// Per streaming warp, behind its ring: probabilities of GR rows, stage tags
-// (task position, page, stream index; 16-byte aligned), stage barriers.
+// bf16 pages with grouped rows go through the tensor cores (mma.sync), the
+// rest through the CUDA cores.
+__host__ __device__ constexpr bool decode_uses_mma(bool bf16, int GR) { return bf16 && GR >= 2; }
+
+// Per streaming warp, behind its ring: probabilities of GR rows (CUDA-core
+// path only), stage tags (task position, page, run, first/last flags;
+// 16-byte aligned), stage barriers.
 template <int GR>
-__host__ __device__ constexpr int decode_warp_bytes(int stages, int stage_bytes) {
-  return (stages * stage_bytes + GR * kDecodeMaxPage * 4 + stages * 8 + stages * 16 + 127) / 128 * 128;
+__host__ __device__ constexpr int decode_warp_bytes(int stages, int stage_bytes, bool mma) {
+  return (stages * stage_bytes + (mma ? 0 : GR * kDecodeMaxPage * 4) + stages * 8 + stages * 16 + 127) / 128 * 128;
+}
+
+// A task of n pages is streamed as nr runs of consecutive pages, run k being
+// pages [run_begin(n, nr, k), run_begin(n, nr, k + 1)): one warp streams a
+// run and deposits one state for it, so claims, deposits and merges happen
+// once per run rather than once per page. nr = max(min(warps, n),
+// ceil(n / run_cap)): every warp gets a run of each task, and runs are at
+// most run_cap pages (1: every page is a run of its own).
+__device__ __forceinline__ int run_begin(int n, int nr, int k) {
+  if (nr == n) return k;  // one page per run
+  const unsigned long long x = (unsigned long long)k * (unsigned)n;
+  return x <= 0xffffffffull ? (int)((unsigned)x / (unsigned)nr) : (int)(x / (unsigned)nr);
 }
 
 // Spins until `ok()` (bounded by `limit` ns; false on timeout or abort).
@@ -300,6 +319,33 @@ __device__ __forceinline__ bool spin_until(F ok, volatile int* abort, uint64_t l
     if ((it & 63u) == 0 && (*abort || global_timer_ns() - t0 > limit)) return false;
     __nanosleep(kSpinSleepNs);
   }
+}
+
+// ---- warp-level tensor-core pieces for grouped rows (bf16) ----------------
+// d += a * b, one m16n8k16 bf16 MMA with fp32 accumulation (a warp-wide
+// instruction): a holds rows g (regs 0, 2) and g + 8 (regs 1, 3) of the
+// 16 x 16 A tile, k pairs 2c (regs 0, 1) and 2c + 8 (regs 2, 3); b holds k
+// pairs 2c and 2c + 8 of column g; d holds columns 2c, 2c + 1 of rows g
+// (0, 1) and g + 8 (2, 3) -- with g = lane / 4, c = lane % 4.
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// Transposes an 8 x 8 b16 block held as one 32-bit fragment word per lane
+// (lane (g, c): row g, columns 2c, 2c + 1).
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+// Two floats as a bf16 pair, rounded to nearest (lo in the low half).
+__device__ __forceinline__ uint32_t bf16x2_rn(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
 }
 
 // log-sum-exp in natural-log units of a row whose merged state is (m, l) in
@@ -327,10 +373,12 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
   volatile int* sFlag = sInts + QD;            // [R] page slot r holds stream page sFlag[r]
   volatile int* sFin = sInts + QD + R;         // [FQ] finisher entry r holds split task sFin[r]
   volatile int* sMerged = sFin + FQ;           // tasks merged (their queue entries are free)
-  volatile int* sMergedPages = sFin + FQ + 1;  // stream pages merged (their slots are free)
+  volatile int* sMergedPages = sFin + FQ + 1;  // stream pages merged (their block ids are free)
   volatile int* sAbort = sFin + FQ + 2;
-  int* sNext = const_cast<int*>(sFin + FQ + 3);  // stream pages claimed
+  int* sNext = const_cast<int*>(sFin + FQ + 3);  // stream runs claimed
   volatile int* sFinAck = sFin + FQ + 4;       // [FQ] finisher entry r was last taken for split task sFinAck[r]
+  volatile int* sMergedRuns = sFinAck + FQ;    // stream runs merged (their slots are free)
+  int* sDone = const_cast<int*>(sMergedRuns + 1);  // stream pages computed
   volatile QueueEntry* sQe = reinterpret_cast<volatile QueueEntry*>(cta + Cta::kEntries);
   volatile FinE* sFe = reinterpret_cast<volatile FinE*>(cta + Cta::kFinish);
   float* sRows = reinterpret_cast<float*>(cta + Cta::kRows);  // [QD][GR][E]
@@ -340,7 +388,8 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
 
   uint8_t* wbase = smem_raw + (size_t)w * p.warp_bytes;
   float* sP = reinterpret_cast<float*>(wbase + (size_t)p.stages * p.stage_bytes);  // [GR][kDecodeMaxPage]
-  int4* sTag = reinterpret_cast<int4*>(sP + GR * kDecodeMaxPage);  // per stage: task position, page, stream page
+  // per stage: task position, page, run, first (1) / last (2) page of the run
+  int4* sTag = reinterpret_cast<int4*>(sP + (decode_uses_mma(Tile::kBF, GR) ? 0 : GR * kDecodeMaxPage));
   uint64_t* sBar = reinterpret_cast<uint64_t*>(sTag + p.stages);
   if (threadIdx.x < 128)
     sInts[threadIdx.x] = (threadIdx.x < QD + R + FQ || (threadIdx.x >= QD + R + FQ + 4 && threadIdx.x < QD + R + 2 * FQ + 4)) ? -1 : 0;
@@ -426,7 +475,9 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
     const int NT = warp_sum_i(NT1) * p.IH;
 
     // Keeps one task staged (grabbed, located, its query rows in registers)
-    // and publishes it while fewer than p.ahead published pages are unclaimed
+    // and publishes it while fewer than p.ahead pages per streaming warp are
+    // published but not yet computed (a CTA commits to little more work than
+    // is in flight, so that the tasks spread evenly at the end of the pool)
     // and a queue entry is free (merged); then stages the next, so the grab's
     // and the loads' latency overlap the wait. Every CTA makes exactly one
     // failing grab; the last one overall resets the counter for the next call.
@@ -496,6 +547,8 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
     stage_next();
     bool staged = true;
     int published = 0;  // pages of the tasks published so far
+    int runs = 0;       // and their runs
+    const int ahead = p.ahead * W;
     auto give_up = [&]() {
       if (lane == 0) {
         atomicOr(p.status, CA_STATUS_TIMEOUT);
@@ -510,7 +563,7 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
     for (int qg = 0;; ++qg) {
       if (!staged) {
         // near the end of the pool: grab only once this CTA needs the task
-        if (!spin_until([&] { return qg - *sMerged < QD && published - *(volatile int*)sNext < p.ahead; }, sAbort, p.wait_ns)) {
+        if (!spin_until([&] { return qg - *sMerged < QD && published - *(volatile int*)sDone < ahead; }, sAbort, p.wait_ns)) {
           give_up();
           break;
         }
@@ -520,7 +573,7 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
       const int sn = sid >= 0 ? st.pg1 - st.pg0 : 0;
       const bool fast = sn <= kDecodeBlkTask;
       if (!spin_until([&] {
-            return qg - *sMerged < QD && published - *(volatile int*)sNext < p.ahead &&
+            return qg - *sMerged < QD && published - *(volatile int*)sDone < ahead &&
                    (!fast || published + sn - *sMergedPages <= kDecodeBlkRing);
           }, sAbort, p.wait_ns)) {
         give_up();
@@ -528,6 +581,7 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
       }
       const int r = qg % QD;
       volatile QueueEntry* e = sQe + r;
+      const int nr = max(min(W, sn), (sn + p.run_cap - 1) / p.run_cap);  // the task's runs
       if (lane == 0) sSeq[r] = -1;  // being rewritten
       __syncwarp();
       __threadfence_block();
@@ -556,6 +610,8 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
           e->pg0 = st.pg0;
           e->n = st.pg1 - st.pg0;
           e->start = published;
+          e->rstart = runs;
+          e->nr = nr;
           e->len = st.len;
           e->raw = st.raw;
           e->apg0 = sapg0;
@@ -564,10 +620,13 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
           e->slot = st.slot;
         }
         published += st.pg1 - st.pg0;
+        runs += nr;
       } else if (lane == 0) {
         e->id = -1;
         e->n = 0;
         e->start = published;
+        e->rstart = runs;
+        e->nr = 0;
       }
       __syncwarp();
       __threadfence_block();
@@ -583,9 +642,9 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
 
   if (w == W) {
     // ================================================================= merger
-    // Combines the page states of each task in page order (so the result
-    // does not depend on which warp streamed which page), frees the page
-    // slots and the queue entry, then writes the output rows, or hands a
+    // Combines the run states of each task in run order (so the result does
+    // not depend on which warp streamed which run), frees the run slots and
+    // the queue entry, then writes the output rows, or hands a
     // split task's states to the finisher.
     // First, while the feeder plans, this warp pulls the query rows and the
     // page table into L2 (the CTAs share the lines out), so that the loads of
@@ -633,7 +692,7 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
       const int id = sQe[r].id;
       if (id < 0) break;
       const int ei = sQe[r].i, eh0 = sQe[r].h0, enr = sQe[r].nrows, eitem = sQe[r].item, entask = sQe[r].ntask,
-                ej = sQe[r].j, en = sQe[r].n, est = sQe[r].start;
+                ej = sQe[r].j, en = sQe[r].n, est = sQe[r].start, erst = sQe[r].rstart, eruns = sQe[r].nr;
       const long long eslot = sQe[r].slot;
       float M[GR], L[GR], o[GR][4];
 #pragma unroll
@@ -643,7 +702,7 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
 #pragma unroll
         for (int cc = 0; cc < 4; ++cc) o[g][cc] = 0.f;
       }
-      for (int gg = est; gg < est + en; ++gg) {
+      for (int gg = erst; gg < erst + eruns; ++gg) {
         const int ps = gg % R;
         if (!spin_until([&] { return sFlag[ps] == gg; }, sAbort, p.wait_ns)) {
           ok = false;
@@ -662,7 +721,7 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
           }
         }
         __syncwarp();
-        if (lane == 0) *sMergedPages = gg + 1;  // slot ps is free
+        if (lane == 0) *sMergedRuns = gg + 1;  // slot ps is free
 #pragma unroll
         for (int g = 0; g < GR; ++g) {
           const float Mn = fmaxf(M[g], mp[g]);
@@ -677,7 +736,10 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
       }
       if (!ok) break;
       __syncwarp();
-      if (lane == 0) *sMerged = q + 1;  // the queue entry is free
+      if (lane == 0) {
+        *sMergedPages = est + en;  // the task's block ids are free
+        *sMerged = q + 1;          // and its queue entry
+      }
       if (entask == 1) {
 #pragma unroll
         for (int g = 0; g < GR; ++g) {
@@ -831,60 +893,107 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
   const char* vc = static_cast<const char*>(p.vc);
   const int vrow_words = E * (int)sizeof(T) / 4;
 
-  // ---- producer: claims the CTA's next page (a shared counter over the pages
-  // of the published tasks, in queue order) whenever the ring has room, and
-  // issues its copies. A claim past the published pages stays pending until
-  // its task is published; a claim past the end marker ends the producer.
-  int g = -1;                 // pending claim (-1: none)
-  bool pdone = false;         // the end marker was reached
-  int cq = 0;                 // queue position the walk is at
-  int c_start = 0, c_n = -1;  // its pages in the stream (c_n < 0: not read)
+  // ---- producer: claims the CTA's next run (a shared counter over the runs
+  // of the published tasks, in queue order) whenever the ring has room and
+  // the last run is issued, and issues its pages' copies one stage at a time,
+  // so the next run's first pages are in flight while this one is computed.
+  // A claim past the published runs stays pending until its task is
+  // published; a claim past the end marker ends the producer.
+  int g = -1;                   // claimed run (-1: none)
+  int gp = -1, gb = 0, ge = 0;  // its next page to issue (-1: not located), first and end page (task pages)
+  bool pdone = false;           // the end marker was reached
+  int cq = 0;                   // queue position the walk is at
+  int c_start = 0, c_n = 0, c_rs = 0, c_nr = -1;  // its first stream page, pages, first run, runs (c_nr < 0: not read)
   int c_i = 0, c_hk = 0, c_pg0 = 0, c_staged = 0;
   unsigned pidx = 0, cidx = 0;  // pages produced / consumed
+  // One query row per item (MHA) streams every page as a run of its own
+  // (the host sets run_cap = 1): run g is stream page g, with no run
+  // bookkeeping on the way.
+  constexpr bool kRuns = GR >= 2;
   auto produce = [&]() {
     while (!pdone && pidx - cidx < (unsigned)p.stages) {
       if (g < 0) {
         int gg = 0;
         if (lane == 0) gg = atomicAdd(sNext, 1);
         g = __shfl_sync(0xffffffffu, gg, 0);
+        gp = -1;
       }
-      // find the task of page g (tasks only move forward)
-      for (;;) {
-        if (c_n < 0) {
-          if (*sMerged > cq) {  // merged already: none of its pages is g
-            ++cq;
-            continue;
+      if (!kRuns) {
+        // find the task of page g (tasks only move forward)
+        for (;;) {
+          if (c_nr < 0) {
+            if (*sMerged > cq) {  // merged already: none of its pages is g
+              ++cq;
+              continue;
+            }
+            const int r = cq % QD;
+            if (sSeq[r] != cq) return;  // not published yet: keep the claim pending
+            __threadfence_block();
+            const int id = sQe[r].id, st = sQe[r].start, n = sQe[r].n;
+            const int ii = sQe[r].i, hh = sQe[r].hk, pg0 = sQe[r].pg0, stg = sQe[r].staged;
+            __threadfence_block();
+            if (sSeq[r] != cq) continue;  // rewritten while read: look again
+            if (id < 0) {
+              pdone = true;
+              return;
+            }
+            c_start = st;
+            c_nr = n;
+            c_i = ii;
+            c_hk = hh;
+            c_pg0 = pg0;
+            c_staged = stg;
           }
-          const int r = cq % QD;
-          if (sSeq[r] != cq) return;  // not published yet: keep the claim pending
-          __threadfence_block();
-          const int id = sQe[r].id, st = sQe[r].start, n = sQe[r].n;
-          const int ii = sQe[r].i, hh = sQe[r].hk, pg0 = sQe[r].pg0, stg = sQe[r].staged;
-          __threadfence_block();
-          if (sSeq[r] != cq) continue;  // rewritten while read: look again
-          if (id < 0) {
-            pdone = true;
-            return;
-          }
-          c_start = st;
-          c_n = n;
-          c_i = ii;
-          c_hk = hh;
-          c_pg0 = pg0;
-          c_staged = stg;
+          if (g < c_start + c_nr) break;
+          ++cq;
+          c_nr = -1;
         }
-        if (g < c_start + c_n) break;
-        ++cq;
-        c_n = -1;
+        gp = g - c_start;
+      } else if (gp < 0) {
+        // find the task of run g (tasks only move forward)
+        for (;;) {
+          if (c_nr < 0) {
+            if (*sMerged > cq) {  // merged already: none of its runs is g
+              ++cq;
+              continue;
+            }
+            const int r = cq % QD;
+            if (sSeq[r] != cq) return;  // not published yet: keep the claim pending
+            __threadfence_block();
+            const int id = sQe[r].id, st = sQe[r].start, n = sQe[r].n, rs = sQe[r].rstart, nr = sQe[r].nr;
+            const int ii = sQe[r].i, hh = sQe[r].hk, pg0 = sQe[r].pg0, stg = sQe[r].staged;
+            __threadfence_block();
+            if (sSeq[r] != cq) continue;  // rewritten while read: look again
+            if (id < 0) {
+              pdone = true;
+              return;
+            }
+            c_start = st;
+            c_n = n;
+            c_rs = rs;
+            c_nr = nr;
+            c_i = ii;
+            c_hk = hh;
+            c_pg0 = pg0;
+            c_staged = stg;
+          }
+          if (g < c_rs + c_nr) break;
+          ++cq;
+          c_nr = -1;
+        }
+        gb = run_begin(c_n, c_nr, g - c_rs);
+        ge = run_begin(c_n, c_nr, g - c_rs + 1);
+        gp = gb;
       }
       const int s = (int)(pidx % (unsigned)p.stages);
-      const int pg = c_pg0 + (g - c_start);
+      const int pg = c_pg0 + gp;
       uint8_t* stage = wbase + (size_t)s * p.stage_bytes;
       if (lane == 0) {
-        sTag[s] = make_int4(cq, pg, g, 0);
+        // tag: task position, page, run, first (1) / last (2) page of the run
+        sTag[s] = make_int4(cq, pg, g, kRuns ? (gp == gb ? 1 : 0) | (gp + 1 == ge ? 2 : 0) : 3);
         int blk;
         if (c_staged) {
-          blk = sBlk[g % kDecodeBlkRing];  // checked by the feeder
+          blk = sBlk[(c_start + gp) % kDecodeBlkRing];  // checked by the feeder
         } else {
           blk = __ldg(p.page_table + (long long)c_i * p.pt_stride + pg);
           if (blk < 0 || blk >= p.num_blocks) {
@@ -893,19 +1002,20 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
           }
         }
         const long long off = ((long long)blk * p.Hk + c_hk) * (long long)p.page_bytes;
+        // the stage's last reads (this warp's shared loads, complete before
+        // the __syncwarp that ended its page) need no proxy fence here
         mbar_arrive_expect_tx(&sBar[s], (uint32_t)(2 * p.page_bytes));
-        fence_proxy_async_smem();
         bulk_g2s(stage, kc + off, (uint32_t)p.page_bytes, &sBar[s], policy);
         bulk_g2s(stage + p.kslot_bytes, vc + off, (uint32_t)p.page_bytes, &sBar[s], policy);
       }
       __syncwarp();
       ++pidx;
-      g = -1;
+      if (!kRuns || ++gp == ge) g = -1;
     }
   };
 
-  // ---- consumer: each page on its own (m, l, acc) per row, deposited in the
-  // page slot of its stream position for the merger
+  // ---- consumer: the pages of a run folded into one running (m, l, acc) per
+  // row, deposited in the run's slot (its stream position) for the merger
   bool failed = false;    // a bounded wait gave up: stop (the other warps stop too)
   unsigned fail_idx = 0;  // the first page not waited for
   int cur = -1;           // task position whose fields are loaded
@@ -913,11 +1023,38 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
     int i, hk, len, raw, apg0, apg1, gw;
   } t = {0, 0, 0, 0, 0, -1, 0};
   const float* sQ = sRows;
+  // bf16 with grouped rows: the page's Q.K^T and P.V run on the tensor cores
+  // (mma.sync m16n8k16, fp32 accumulation) as S^T = K Q^T and O^T = V^T P^T,
+  // the keys and the head dims on the 16-wide M side and the group's rows on
+  // the 8-wide N side (rows past GR are zero padding). K's A fragments come
+  // straight from the dim-pair-major page (one 64-bit load gives two keys of
+  // a dim pair); S^T's accumulator, rounded to bf16 and transposed in
+  // registers (movmatrix), is P^T's B fragment; V's A fragments are 128-bit
+  // row loads transposed the same way. P enters as bf16 plus its rounding
+  // residual (two MMAs), so the weights keep ~16 bits like the fp32
+  // probabilities of the CUDA-core path. A page costs ~250 instructions
+  // instead of ~1600 at eight rows. MHA (GR = 1) and fp32 keep the CUDA-core
+  // path.
+  constexpr bool kMMA = decode_uses_mma(Tile::kBF, GR);
+  constexpr int NKS = E / 16;  // k-steps over the head dim
+  constexpr int NT = E / 16;   // 16-dim tiles of O^T
+  uint32_t qb[NKS][2];         // the task's Q as B fragments: row g, dims 16ks + 2c (+1) and 16ks + 8 + 2c (+1)
+#pragma unroll
+  for (int ks = 0; ks < NKS; ++ks) qb[ks][0] = qb[ks][1] = 0u;
   // K.q accumulation chains per row: four for one row, fewer as the rows
   // themselves give independent chains
   constexpr int CH = GR >= 4 ? 1 : 4 / GR;
   constexpr int NS = kDecodeMaxPage / 32;
   constexpr int UQK = GR == 1 ? 8 : 4;  // unroll of the K-row loops
+  // the run's state: CUDA-core path: acc (4 dims per lane), the running max
+  // and this lane's part of the sum per row; tensor-core path: O^T tiles
+  // (16 dims x 8 rows; tile 2sg + jp holds dims 32sg + 8(g / 2) + 4jp + g % 2
+  // (regs 0, 1) and + 2 (regs 2, 3) of rows 2c (regs 0, 2) and 2c + 1 (regs
+  // 1, 3)), rows 2c and 2c + 1's running max and this lane's part of their sums
+  float acc[GR][4];
+  float m[GR], lpart[GR];
+  float mo[kMMA ? NT : 1][4];
+  float mrow[2], lrow[2];
   for (;;) {
     produce();
     if (pidx == cidx) {
@@ -945,14 +1082,37 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
       t.apg1 = sQe[r].apg1;
       t.gw = sQe[r].gw;
       sQ = sRows + r * GR * E;
+      if constexpr (kMMA) {
+        const int gq = lane >> 2, cq4 = lane & 3;
+#pragma unroll
+        for (int ks = 0; ks < NKS; ++ks) {
+          if (gq < GR) {
+            const float2 lo = *reinterpret_cast<const float2*>(sQ + gq * E + 16 * ks + 2 * cq4);
+            const float2 hi = *reinterpret_cast<const float2*>(sQ + gq * E + 16 * ks + 8 + 2 * cq4);
+            qb[ks][0] = bf16x2_rn(lo.x, lo.y);  // exact: q is bf16
+            qb[ks][1] = bf16x2_rn(hi.x, hi.y);
+          } else {
+            qb[ks][0] = qb[ks][1] = 0u;
+          }
+        }
+      }
     }
-    float acc[GR][4];
-    float m[GR], lpart[GR];
+    const bool fresh = !kRuns || (tag.w & 1);  // the run's first page
+    if (fresh) {
+      if constexpr (kMMA) {
 #pragma unroll
-    for (int gr = 0; gr < GR; ++gr) {
-      lpart[gr] = 0.f;
+        for (int tt = 0; tt < NT; ++tt) mo[tt][0] = mo[tt][1] = mo[tt][2] = mo[tt][3] = 0.f;
+        mrow[0] = mrow[1] = -INFINITY;
+        lrow[0] = lrow[1] = 0.f;
+      } else {
 #pragma unroll
-      for (int cc = 0; cc < 4; ++cc) acc[gr][cc] = 0.f;
+        for (int gr = 0; gr < GR; ++gr) {
+          m[gr] = -INFINITY;
+          lpart[gr] = 0.f;
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) acc[gr][cc] = 0.f;
+        }
+      }
     }
     {
       const uint32_t parity = (cidx / (unsigned)p.stages) & 1u;
@@ -994,208 +1154,350 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
         __syncwarp();
       }
 
-      // ---- Q.K^T for the page's ntok keys, every row
-      const uint32_t* sK = reinterpret_cast<const uint32_t*>(stage);
-      const int nsteps = (ntok + 31) >> 5;
-      float x[GR][NS];
-      float mc[GR];
+      if constexpr (kMMA) {
+        // S^T = K Q^T and O^T = V^T P^T on m16n8k16 tiles: the page's keys
+        // and the head dims are the M sides, the group's rows the N side.
+        // Lane (g, c) = (lane / 4, lane % 4) holds rows 2c, 2c + 1.
+        const int gq = lane >> 2, cq4 = lane & 3;
+        const uint32_t* sK = reinterpret_cast<const uint32_t*>(stage);
+        const uint8_t* sVb = stage + p.kslot_bytes;
+        const int nkb = (ntok + 15) >> 4;  // 16-key blocks
+        for (int kb = 0; kb < nkb; ++kb) {
+          // A = K: M row g is key kA, row g + 8 key kA + 1, so one 64-bit
+          // load gives both; k pair c is dim pair 8ks + c, pair c + 4 is
+          // 8ks + 4 + c, matching the Q fragments
+          const int kA = 16 * kb + 2 * gq;
+          float sc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int gr = 0; gr < GR; ++gr) {
-        mc[gr] = -INFINITY;
+          for (int ks = 0; ks < NKS; ++ks) {
+            const uint2 w0 = *reinterpret_cast<const uint2*>(sK + (8 * ks + cq4) * p.page + kA);
+            const uint2 w1 = *reinterpret_cast<const uint2*>(sK + (8 * ks + 4 + cq4) * p.page + kA);
+            const uint32_t a[4] = {w0.x, w0.y, w1.x, w1.y};
+            mma_bf16_16816(sc, a, qb[ks][0], qb[ks][1]);
+          }
+          // sc: (key kA; rows 2c, 2c + 1), (key kA + 1; rows 2c, 2c + 1)
+          const bool v0 = kA < ntok, v1 = kA + 1 < ntok;
+          float x[2][2];  // [key kA / kA + 1][row 2c / 2c + 1], log2 units
+          x[0][0] = v0 ? sc[0] * p.c : -INFINITY;
+          x[0][1] = v0 ? sc[1] * p.c : -INFINITY;
+          x[1][0] = v1 ? sc[2] * p.c : -INFINITY;
+          x[1][1] = v1 ? sc[3] * p.c : -INFINITY;
+          float alpha[2], pk[2][2];
 #pragma unroll
-        for (int stp = 0; stp < NS; ++stp) x[gr][stp] = -INFINITY;
-      }
-      if (p.page == 16) {
-        // a 16-key page: lanes t and 16+t share key t, each half-warp takes
-        // every other K row (conflict-free: banks 16*half + t)
-        const int tk = lane & 15, hh = lane >> 4;
-        const uint32_t* kp = sK + tk;
-        float a[GR][CH];
+          for (int r = 0; r < 2; ++r) {
+            float bm = fmaxf(x[0][r], x[1][r]);
+            bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 4));
+            bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 8));
+            bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 16));
+            const float mn = fmaxf(mrow[r], bm);  // finite: key 16kb is valid
+            alpha[r] = exp2_approx(mrow[r] - mn);  // mrow = -inf: 0
+            mrow[r] = mn;
+            pk[0][r] = exp2_approx(x[0][r] - mn);
+            pk[1][r] = exp2_approx(x[1][r] - mn);
+            lrow[r] = fmaf(lrow[r], alpha[r], pk[0][r] + pk[1][r]);  // this lane's keys only
+          }
+          if (kb > 0 || !fresh) {
 #pragma unroll
-        for (int gr = 0; gr < GR; ++gr)
+            for (int tt = 0; tt < NT; ++tt) {
+              mo[tt][0] *= alpha[0];
+              mo[tt][1] *= alpha[1];
+              mo[tt][2] *= alpha[0];
+              mo[tt][3] *= alpha[1];
+            }
+          }
+          // B = P^T: transposing the 8 x 8 (key, row) blocks of P gives
+          // lane (g, c) row g at keys 16kb + 4c (+2) (from the kA block) and
+          // 16kb + 4c + 1 (+3) (the kA + 1 block), which fixes the k order of
+          // the V fragments below. P enters as bf16 + its rounding residual.
+          uint32_t ph[2], pl[2];
 #pragma unroll
-          for (int c = 0; c < CH; ++c) a[gr][c] = 0.f;
-        if constexpr (Tile::kBF) {
+          for (int h = 0; h < 2; ++h) {
+            const uint32_t hi = bf16x2_rn(pk[h][0], pk[h][1]);
+            const uint32_t lo = bf16x2_rn(pk[h][0] - bf16_lo(hi), pk[h][1] - bf16_hi(hi));
+            ph[h] = movmatrix_trans(hi);
+            pl[h] = movmatrix_trans(lo);
+          }
+          // A = V^T: lane (g, c') loads 8 dims (32sg + 8c' ..) of keys
+          // 16kb + 2g (h = 0) and + 1 (h = 1); word j of those loads, as an
+          // 8 x 8 (key, dim) block, transposes into M rows g <-> dim
+          // 32sg + 8(g / 2) + 2j + g % 2 at keys 16kb + 4c (+2) (+h). Keys
+          // past ntok load as zeros (P is 0 there, but 0 * NaN is not 0).
+#pragma unroll
+          for (int sg = 0; sg < E / 32; ++sg) {
+            uint4 vw[2];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int kv = 16 * kb + 2 * gq + h;
+              vw[h] = kv < ntok ? *reinterpret_cast<const uint4*>(sVb + ((size_t)kv * E + 32 * sg + 8 * cq4) * 2)
+                                : make_uint4(0u, 0u, 0u, 0u);
+            }
+            const uint32_t xt[2][4] = {
+                {movmatrix_trans(vw[0].x), movmatrix_trans(vw[0].y), movmatrix_trans(vw[0].z), movmatrix_trans(vw[0].w)},
+                {movmatrix_trans(vw[1].x), movmatrix_trans(vw[1].y), movmatrix_trans(vw[1].z), movmatrix_trans(vw[1].w)}};
+#pragma unroll
+            for (int jp = 0; jp < 2; ++jp) {
+              const uint32_t a[4] = {xt[0][2 * jp], xt[0][2 * jp + 1], xt[1][2 * jp], xt[1][2 * jp + 1]};
+              mma_bf16_16816(mo[2 * sg + jp], a, ph[0], ph[1]);
+              mma_bf16_16816(mo[2 * sg + jp], a, pl[0], pl[1]);
+            }
+          }
+        }
+        __syncwarp();  // every lane is done with stage s
+        ++cidx;
+        if (lane == 0) atomicAdd(sDone, 1);
+      } else {
+        // ---- Q.K^T for the page's ntok keys, every row
+        const uint32_t* sK = reinterpret_cast<const uint32_t*>(stage);
+        const int nsteps = (ntok + 31) >> 5;
+        float x[GR][NS];
+        float mc[GR];
+#pragma unroll
+        for (int gr = 0; gr < GR; ++gr) {
+          mc[gr] = -INFINITY;
+#pragma unroll
+          for (int stp = 0; stp < NS; ++stp) x[gr][stp] = -INFINITY;
+        }
+        if (p.page == 16) {
+          // a 16-key page: lanes t and 16+t share key t, each half-warp takes
+          // every other K row (conflict-free: banks 16*half + t)
+          const int tk = lane & 15, hh = lane >> 4;
+          const uint32_t* kp = sK + tk;
+          float a[GR][CH];
+#pragma unroll
+          for (int gr = 0; gr < GR; ++gr)
+#pragma unroll
+            for (int c = 0; c < CH; ++c) a[gr][c] = 0.f;
+          if constexpr (Tile::kBF) {
 #pragma unroll UQK
-          for (int r = hh; r < Tile::kRows; r += 4) {
-            const uint32_t w0 = kp[r * 16];
-            const uint32_t w1 = kp[(r + 2) * 16];
-            const float k0 = bf16_lo(w0), k1 = bf16_hi(w0), k2 = bf16_lo(w1), k3 = bf16_hi(w1);
+            for (int r = hh; r < Tile::kRows; r += 4) {
+              const uint32_t w0 = kp[r * 16];
+              const uint32_t w1 = kp[(r + 2) * 16];
+              const float k0 = bf16_lo(w0), k1 = bf16_hi(w0), k2 = bf16_lo(w1), k3 = bf16_hi(w1);
+#pragma unroll
+              for (int gr = 0; gr < GR; ++gr) {
+                const float2* q2 = reinterpret_cast<const float2*>(sQ + gr * E);
+                const float2 q0 = q2[r], q1 = q2[r + 2];
+                a[gr][0 % CH] = fmaf(k0, q0.x, a[gr][0 % CH]);
+                a[gr][1 % CH] = fmaf(k1, q0.y, a[gr][1 % CH]);
+                a[gr][2 % CH] = fmaf(k2, q1.x, a[gr][2 % CH]);
+                a[gr][3 % CH] = fmaf(k3, q1.y, a[gr][3 % CH]);
+              }
+            }
+          } else {
+            const float* kf = reinterpret_cast<const float*>(kp);
+#pragma unroll UQK
+            for (int r = hh; r < Tile::kRows; r += 8) {
+              const float k0 = kf[r * 16], k1 = kf[(r + 2) * 16], k2 = kf[(r + 4) * 16], k3 = kf[(r + 6) * 16];
+#pragma unroll
+              for (int gr = 0; gr < GR; ++gr) {
+                const float* qf = sQ + gr * E;
+                a[gr][0 % CH] = fmaf(k0, qf[r], a[gr][0 % CH]);
+                a[gr][1 % CH] = fmaf(k1, qf[r + 2], a[gr][1 % CH]);
+                a[gr][2 % CH] = fmaf(k2, qf[r + 4], a[gr][2 % CH]);
+                a[gr][3 % CH] = fmaf(k3, qf[r + 6], a[gr][3 % CH]);
+              }
+            }
+          }
+#pragma unroll
+          for (int gr = 0; gr < GR; ++gr) {
+            float logit;
+            if constexpr (CH == 4)
+              logit = (a[gr][0] + a[gr][1]) + (a[gr][2] + a[gr][3]);
+            else if constexpr (CH == 2)
+              logit = a[gr][0] + a[gr][1];
+            else
+              logit = a[gr][0];
+            logit += __shfl_xor_sync(0xffffffffu, logit, 16);
+            x[gr][0] = (tk < ntok && hh == 0) ? logit * p.c : -INFINITY;
+            mc[gr] = x[gr][0];
+          }
+        } else {
+#pragma unroll
+          for (int stp = 0; stp < NS; ++stp) {
+            if (stp < nsteps) {
+              const int j = stp * 32 + lane;
+              const uint32_t* kp = sK + min(j, ntok - 1);
+              float a[GR][CH];
+#pragma unroll
+              for (int gr = 0; gr < GR; ++gr)
+#pragma unroll
+                for (int c = 0; c < CH; ++c) a[gr][c] = 0.f;
+              if constexpr (Tile::kBF) {
+#pragma unroll UQK
+                for (int r = 0; r < Tile::kRows; r += 2) {
+                  const uint32_t w0 = kp[r * p.page];
+                  const uint32_t w1 = kp[(r + 1) * p.page];
+                  const float k0 = bf16_lo(w0), k1 = bf16_hi(w0), k2 = bf16_lo(w1), k3 = bf16_hi(w1);
+#pragma unroll
+                  for (int gr = 0; gr < GR; ++gr) {
+                    const float4 qq = reinterpret_cast<const float4*>(sQ + gr * E)[r >> 1];
+                    a[gr][0 % CH] = fmaf(k0, qq.x, a[gr][0 % CH]);
+                    a[gr][1 % CH] = fmaf(k1, qq.y, a[gr][1 % CH]);
+                    a[gr][2 % CH] = fmaf(k2, qq.z, a[gr][2 % CH]);
+                    a[gr][3 % CH] = fmaf(k3, qq.w, a[gr][3 % CH]);
+                  }
+                }
+              } else {
+                const float* kf = reinterpret_cast<const float*>(kp);
+#pragma unroll UQK
+                for (int r = 0; r < Tile::kRows; r += 4) {
+                  const float k0 = kf[r * p.page], k1 = kf[(r + 1) * p.page], k2 = kf[(r + 2) * p.page],
+                              k3 = kf[(r + 3) * p.page];
+#pragma unroll
+                  for (int gr = 0; gr < GR; ++gr) {
+                    const float4 qq = reinterpret_cast<const float4*>(sQ + gr * E)[r >> 2];
+                    a[gr][0 % CH] = fmaf(k0, qq.x, a[gr][0 % CH]);
+                    a[gr][1 % CH] = fmaf(k1, qq.y, a[gr][1 % CH]);
+                    a[gr][2 % CH] = fmaf(k2, qq.z, a[gr][2 % CH]);
+                    a[gr][3 % CH] = fmaf(k3, qq.w, a[gr][3 % CH]);
+                  }
+                }
+              }
+#pragma unroll
+              for (int gr = 0; gr < GR; ++gr) {
+                float logit;
+                if constexpr (CH == 4)
+                  logit = (a[gr][0] + a[gr][1]) + (a[gr][2] + a[gr][3]);
+                else if constexpr (CH == 2)
+                  logit = a[gr][0] + a[gr][1];
+                else
+                  logit = a[gr][0];
+                x[gr][stp] = (j < ntok) ? logit * p.c : -INFINITY;
+                mc[gr] = fmaxf(mc[gr], x[gr][stp]);
+              }
+            }
+          }
+        }
+        // ---- softmax of the page on the run's running maximum, per row
+#pragma unroll
+        for (int gr = 0; gr < GR; ++gr) {
+          const float mn = fmaxf(m[gr], warp_max(mc[gr]));  // finite: the page has a key
+          if (!fresh) {
+            const float al = exp2_approx(m[gr] - mn);
+            lpart[gr] *= al;
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) acc[gr][cc] *= al;
+          }
+          m[gr] = mn;
+#pragma unroll
+          for (int stp = 0; stp < NS; ++stp) {
+            if (stp < nsteps) {
+              const float pr = exp2_approx(x[gr][stp] - m[gr]);
+              sP[gr * kDecodeMaxPage + stp * 32 + lane] = pr;
+              lpart[gr] += pr;
+            }
+          }
+        }
+        __syncwarp();
+        // ---- P.V over exactly ntok keys
+        const uint32_t* vb = reinterpret_cast<const uint32_t*>(stage + p.kslot_bytes);
+        if constexpr (Tile::kBF) {
+#pragma unroll 4
+          for (int tt = tg; tt < ntok; tt += Tile::kKeysPerStep) {
+            const uint2 wv = *reinterpret_cast<const uint2*>(vb + tt * vrow_words + dg * 2);
+            const float v0 = bf16_lo(wv.x), v1 = bf16_hi(wv.x), v2 = bf16_lo(wv.y), v3 = bf16_hi(wv.y);
 #pragma unroll
             for (int gr = 0; gr < GR; ++gr) {
-              const float2* q2 = reinterpret_cast<const float2*>(sQ + gr * E);
-              const float2 q0 = q2[r], q1 = q2[r + 2];
-              a[gr][0 % CH] = fmaf(k0, q0.x, a[gr][0 % CH]);
-              a[gr][1 % CH] = fmaf(k1, q0.y, a[gr][1 % CH]);
-              a[gr][2 % CH] = fmaf(k2, q1.x, a[gr][2 % CH]);
-              a[gr][3 % CH] = fmaf(k3, q1.y, a[gr][3 % CH]);
+              const float pj = sP[gr * kDecodeMaxPage + tt];
+              acc[gr][0] = fmaf(pj, v0, acc[gr][0]);
+              acc[gr][1] = fmaf(pj, v1, acc[gr][1]);
+              acc[gr][2] = fmaf(pj, v2, acc[gr][2]);
+              acc[gr][3] = fmaf(pj, v3, acc[gr][3]);
             }
           }
         } else {
-          const float* kf = reinterpret_cast<const float*>(kp);
-#pragma unroll UQK
-          for (int r = hh; r < Tile::kRows; r += 8) {
-            const float k0 = kf[r * 16], k1 = kf[(r + 2) * 16], k2 = kf[(r + 4) * 16], k3 = kf[(r + 6) * 16];
+#pragma unroll 4
+          for (int tt = tg; tt < ntok; tt += Tile::kKeysPerStep) {
+            const float4 wv = *reinterpret_cast<const float4*>(vb + tt * vrow_words + dg * 4);
 #pragma unroll
             for (int gr = 0; gr < GR; ++gr) {
-              const float* qf = sQ + gr * E;
-              a[gr][0 % CH] = fmaf(k0, qf[r], a[gr][0 % CH]);
-              a[gr][1 % CH] = fmaf(k1, qf[r + 2], a[gr][1 % CH]);
-              a[gr][2 % CH] = fmaf(k2, qf[r + 4], a[gr][2 % CH]);
-              a[gr][3 % CH] = fmaf(k3, qf[r + 6], a[gr][3 % CH]);
+              const float pj = sP[gr * kDecodeMaxPage + tt];
+              acc[gr][0] = fmaf(pj, wv.x, acc[gr][0]);
+              acc[gr][1] = fmaf(pj, wv.y, acc[gr][1]);
+              acc[gr][2] = fmaf(pj, wv.z, acc[gr][2]);
+              acc[gr][3] = fmaf(pj, wv.w, acc[gr][3]);
             }
           }
         }
-#pragma unroll
-        for (int gr = 0; gr < GR; ++gr) {
-          float logit;
-          if constexpr (CH == 4)
-            logit = (a[gr][0] + a[gr][1]) + (a[gr][2] + a[gr][3]);
-          else if constexpr (CH == 2)
-            logit = a[gr][0] + a[gr][1];
-          else
-            logit = a[gr][0];
-          logit += __shfl_xor_sync(0xffffffffu, logit, 16);
-          x[gr][0] = (tk < ntok && hh == 0) ? logit * p.c : -INFINITY;
-          mc[gr] = x[gr][0];
-        }
-      } else {
-#pragma unroll
-        for (int stp = 0; stp < NS; ++stp) {
-          if (stp < nsteps) {
-            const int j = stp * 32 + lane;
-            const uint32_t* kp = sK + min(j, ntok - 1);
-            float a[GR][CH];
-#pragma unroll
-            for (int gr = 0; gr < GR; ++gr)
-#pragma unroll
-              for (int c = 0; c < CH; ++c) a[gr][c] = 0.f;
-            if constexpr (Tile::kBF) {
-#pragma unroll UQK
-              for (int r = 0; r < Tile::kRows; r += 2) {
-                const uint32_t w0 = kp[r * p.page];
-                const uint32_t w1 = kp[(r + 1) * p.page];
-                const float k0 = bf16_lo(w0), k1 = bf16_hi(w0), k2 = bf16_lo(w1), k3 = bf16_hi(w1);
-#pragma unroll
-                for (int gr = 0; gr < GR; ++gr) {
-                  const float4 qq = reinterpret_cast<const float4*>(sQ + gr * E)[r >> 1];
-                  a[gr][0 % CH] = fmaf(k0, qq.x, a[gr][0 % CH]);
-                  a[gr][1 % CH] = fmaf(k1, qq.y, a[gr][1 % CH]);
-                  a[gr][2 % CH] = fmaf(k2, qq.z, a[gr][2 % CH]);
-                  a[gr][3 % CH] = fmaf(k3, qq.w, a[gr][3 % CH]);
-                }
-              }
-            } else {
-              const float* kf = reinterpret_cast<const float*>(kp);
-#pragma unroll UQK
-              for (int r = 0; r < Tile::kRows; r += 4) {
-                const float k0 = kf[r * p.page], k1 = kf[(r + 1) * p.page], k2 = kf[(r + 2) * p.page],
-                            k3 = kf[(r + 3) * p.page];
-#pragma unroll
-                for (int gr = 0; gr < GR; ++gr) {
-                  const float4 qq = reinterpret_cast<const float4*>(sQ + gr * E)[r >> 2];
-                  a[gr][0 % CH] = fmaf(k0, qq.x, a[gr][0 % CH]);
-                  a[gr][1 % CH] = fmaf(k1, qq.y, a[gr][1 % CH]);
-                  a[gr][2 % CH] = fmaf(k2, qq.z, a[gr][2 % CH]);
-                  a[gr][3 % CH] = fmaf(k3, qq.w, a[gr][3 % CH]);
-                }
-              }
-            }
-#pragma unroll
-            for (int gr = 0; gr < GR; ++gr) {
-              float logit;
-              if constexpr (CH == 4)
-                logit = (a[gr][0] + a[gr][1]) + (a[gr][2] + a[gr][3]);
-              else if constexpr (CH == 2)
-                logit = a[gr][0] + a[gr][1];
-              else
-                logit = a[gr][0];
-              x[gr][stp] = (j < ntok) ? logit * p.c : -INFINITY;
-              mc[gr] = fmaxf(mc[gr], x[gr][stp]);
-            }
-          }
-        }
+        __syncwarp();  // every lane is done with stage s
+        ++cidx;
+        if (lane == 0) atomicAdd(sDone, 1);
       }
-      // ---- softmax of the page on its own maximum, per row
+    }
+    produce();  // the stage is free: refill it before depositing
+    if (kRuns && !(tag.w & 2)) continue;  // the run goes on
+    if constexpr (kMMA) {
+      // rows 2c, 2c + 1: sums over the eight lanes of column c; the maxima
+      // are already uniform there
+      const int gq = lane >> 2, cq4 = lane & 3;
 #pragma unroll
-      for (int gr = 0; gr < GR; ++gr) {
-        m[gr] = warp_max(mc[gr]);
+      for (int r = 0; r < 2; ++r) {
+        lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 4);
+        lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 8);
+        lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 16);
+      }
+      const int gz = tag.z;
+      if (!spin_until([&] { return *sMergedRuns > gz - R; }, sAbort, p.wait_ns)) {
+        failed = true;
+        fail_idx = cidx;
+        break;
+      }
+      float* slot = sPage + (gz % R) * GR * RS;
+      if (2 * cq4 < GR) {
+        float* r0 = slot + (2 * cq4) * RS;
+        float* r1 = r0 + RS;
 #pragma unroll
-        for (int stp = 0; stp < NS; ++stp) {
-          if (stp < nsteps) {
-            const float pr = exp2_approx(x[gr][stp] - m[gr]);
-            sP[gr * kDecodeMaxPage + stp * 32 + lane] = pr;
-            lpart[gr] += pr;
-          }
+        for (int tt = 0; tt < NT; ++tt) {
+          const int d = 32 * (tt >> 1) + 8 * (gq >> 1) + 4 * (tt & 1) + (gq & 1);
+          r0[d] = mo[tt][0];
+          r1[d] = mo[tt][1];
+          r0[d + 2] = mo[tt][2];
+          r1[d + 2] = mo[tt][3];
+        }
+        if (gq == 0) {
+          r0[E] = mrow[0];
+          r0[E + 1] = lrow[0];
+          r1[E] = mrow[1];
+          r1[E + 1] = lrow[1];
         }
       }
       __syncwarp();
-      // ---- P.V over exactly ntok keys
-      const uint32_t* vb = reinterpret_cast<const uint32_t*>(stage + p.kslot_bytes);
-      if constexpr (Tile::kBF) {
-#pragma unroll 4
-        for (int tt = tg; tt < ntok; tt += Tile::kKeysPerStep) {
-          const uint2 wv = *reinterpret_cast<const uint2*>(vb + tt * vrow_words + dg * 2);
-          const float v0 = bf16_lo(wv.x), v1 = bf16_hi(wv.x), v2 = bf16_lo(wv.y), v3 = bf16_hi(wv.y);
+      __threadfence_block();
+      if (lane == 0) sFlag[gz % R] = gz;
+    } else {
+      // ---- deposit the run's states in slot tag.z % R once the merger is past
+      // the run that held it before
+      float l[GR];
 #pragma unroll
-          for (int gr = 0; gr < GR; ++gr) {
-            const float pj = sP[gr * kDecodeMaxPage + tt];
-            acc[gr][0] = fmaf(pj, v0, acc[gr][0]);
-            acc[gr][1] = fmaf(pj, v1, acc[gr][1]);
-            acc[gr][2] = fmaf(pj, v2, acc[gr][2]);
-            acc[gr][3] = fmaf(pj, v3, acc[gr][3]);
-          }
-        }
-      } else {
-#pragma unroll 4
-        for (int tt = tg; tt < ntok; tt += Tile::kKeysPerStep) {
-          const float4 wv = *reinterpret_cast<const float4*>(vb + tt * vrow_words + dg * 4);
+      for (int gr = 0; gr < GR; ++gr) {
+        l[gr] = warp_sum(lpart[gr]);
 #pragma unroll
-          for (int gr = 0; gr < GR; ++gr) {
-            const float pj = sP[gr * kDecodeMaxPage + tt];
-            acc[gr][0] = fmaf(pj, wv.x, acc[gr][0]);
-            acc[gr][1] = fmaf(pj, wv.y, acc[gr][1]);
-            acc[gr][2] = fmaf(pj, wv.z, acc[gr][2]);
-            acc[gr][3] = fmaf(pj, wv.w, acc[gr][3]);
-          }
+        for (int o = Tile::kLanesPerKey; o < 32; o <<= 1) {
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) acc[gr][cc] += __shfl_xor_sync(0xffffffffu, acc[gr][cc], o);
         }
       }
-      __syncwarp();  // every lane is done with stage s
-      ++cidx;
-    }
-    produce();  // the stage is free: refill it before depositing
-    // ---- deposit the page's states in slot tag.z % R once the merger is past
-    // the page that held it before
-    float l[GR];
-#pragma unroll
-    for (int gr = 0; gr < GR; ++gr) {
-      l[gr] = warp_sum(lpart[gr]);
-#pragma unroll
-      for (int o = Tile::kLanesPerKey; o < 32; o <<= 1) {
-#pragma unroll
-        for (int cc = 0; cc < 4; ++cc) acc[gr][cc] += __shfl_xor_sync(0xffffffffu, acc[gr][cc], o);
+      const int gz = tag.z;
+      if (!spin_until([&] { return *sMergedRuns > gz - R; }, sAbort, p.wait_ns)) {
+        failed = true;
+        fail_idx = cidx;
+        break;
       }
-    }
-    const int gz = tag.z;
-    if (!spin_until([&] { return *sMergedPages > gz - R; }, sAbort, p.wait_ns)) {
-      failed = true;
-      fail_idx = cidx;
-      break;
-    }
-    float* slot = sPage + (gz % R) * GR * RS;
+      float* slot = sPage + (gz % R) * GR * RS;
 #pragma unroll
-    for (int gr = 0; gr < GR; ++gr) {
-      if (lane < Tile::kLanesPerKey)
-        *reinterpret_cast<float4*>(slot + gr * RS + dg * 4) =
-            make_float4(acc[gr][0], acc[gr][1], acc[gr][2], acc[gr][3]);
-      if (lane == 0) {
-        slot[gr * RS + E] = m[gr];
-        slot[gr * RS + E + 1] = l[gr];
+      for (int gr = 0; gr < GR; ++gr) {
+        if (lane < Tile::kLanesPerKey)
+          *reinterpret_cast<float4*>(slot + gr * RS + dg * 4) =
+              make_float4(acc[gr][0], acc[gr][1], acc[gr][2], acc[gr][3]);
+        if (lane == 0) {
+          slot[gr * RS + E] = m[gr];
+          slot[gr * RS + E + 1] = l[gr];
+        }
       }
+      __syncwarp();
+      __threadfence_block();
+      if (lane == 0) sFlag[gz % R] = gz;
     }
-    __syncwarp();
-    __threadfence_block();
-    if (lane == 0) sFlag[gz % R] = gz;
   }
   if (failed && lane == 0) {
     atomicOr(p.status, CA_STATUS_TIMEOUT);
