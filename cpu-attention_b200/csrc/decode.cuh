@@ -37,14 +37,15 @@
 //         warps are about to need it: an entry (item, pages, position in the
 //         CTA's page stream), the query rows in fp32 and the block ids in a
 //         ring. Near the end of the pool it grabs only when needed.
-//       - streaming warps claim pages of the CTA's page stream one at a time
+//       - streaming warps claim runs of the CTA's run stream one at a time
 //         (a shared counter), so every warp stays busy whatever the task
-//         sizes. A claimed page's K and V arrive by 1-D bulk copies
-//         (cp.async.bulk, the TMA engine; L2 evict-first) into the warp's own
-//         ring of stages, completing on one mbarrier per stage. The warp
-//         computes the page's (m, l, acc) of each row and deposits them in the
-//         page's slot of a ring.
-//       - the merger folds the page states of each task in page order, then
+//         sizes: a run is one page for one-row items (MHA) and about a
+//         warp's share of the task for grouped rows. A run's pages' K and V
+//         arrive by 1-D bulk copies (cp.async.bulk, the TMA engine; L2
+//         evict-first) into the warp's own ring of stages, completing on one
+//         mbarrier per stage. The warp folds the run's pages into one
+//         (m, l, acc) per row and deposits it in the run's slot of a ring.
+//       - the merger folds the run states of each task in run order, then
 //         writes the output rows, or hands a split task's states on.
 //       - the finishers write a split task's partials (m, l, acc) to the
 //         workspace and take the item's ticket; the item's last task merges
@@ -52,7 +53,9 @@
 //   * Q.K^T: lane = key, reading the dim-pair-major K page with conflict-free
 //     32-bit shared loads (a 16-key page: half-warps split the K rows) against
 //     the fp32 query rows as broadcast loads, each K word feeding every row;
-//     P.V: lanes own 4 dims of a V row, each V word feeding every row.
+//     P.V: lanes own 4 dims of a V row, each V word feeding every row. bf16
+//     with grouped rows runs both on mma.sync tiles instead (see the
+//     streaming warp).
 //   * Masked keys never reach P.V (the loop stops at the last valid key), so
 //     NaN in unused slots of a page cannot leak (`paged_attn.mojo:686-687`).
 //   * Start-up: the first copies wait for three dependent round trips (the
