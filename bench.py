@@ -531,20 +531,58 @@ def make_workload(name, rank, world, dev):
 
 # --------------------------------------------------------------------- timing --
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 50 ms; each
-    workload reads the samples of its own time window."""
+    """SM clocks and throttle reasons sampled during the run; each workload
+    reads the samples of its own time window. NVML (read-only queries) from a
+    background thread every 5 ms, so that even a timed region of a few
+    milliseconds holds samples; `nvidia-smi -lms 50` when NVML is missing."""
 
     FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
     def __init__(self, gpus):
         self.proc = None
         self.path = None
         self.gpus = gpus
+        self.thread = None
+        self.samples = []  # (wall time, sm MHz, max sm MHz, reason names)
+
+    def _nvml_loop(self, nv, handles, bits):
+        reasons_of = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        maxes = [nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM) for h in handles]
+        while not self.halt.is_set():
+            t = time.time()
+            for h, mx in zip(handles, maxes):
+                try:
+                    sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                    r = reasons_of(h)
+                except nv.NVMLError:
+                    continue
+                self.samples.append((t, float(sm), float(mx), {n for n, b in bits if r & b}))
+            self.halt.wait(0.005)
 
     def start(self):
         """Start sampling; returns once the first sample is in (at most ~5 s)."""
+        try:
+            import threading
+            import pynvml as nv
+            nv.nvmlInit()
+            handles = [nv.nvmlDeviceGetHandleByIndex(g) for g in self.gpus]
+            pre = "nvmlClocksEventReason" if hasattr(nv, "nvmlClocksEventReasonHwSlowdown") else "nvmlClocksThrottleReason"
+            bits = [(n, getattr(nv, pre + k)) for n, k in zip(
+                self.NAMES, ["HwSlowdown", "HwThermalSlowdown", "SwThermalSlowdown", "SwPowerCap"])]
+            self.halt = threading.Event()
+            self.thread = threading.Thread(target=self._nvml_loop, args=(nv, handles, bits), daemon=True)
+            self.thread.start()
+            self.nv = nv
+            t0 = time.time()
+            while not self.samples and time.time() - t0 < 5.0:
+                time.sleep(0.01)
+            return
+        except Exception:  # no NVML: fall back to nvidia-smi
+            self.thread = None
         try:
             fd, self.path = tempfile.mkstemp(suffix=".csv")
             os.close(fd)
@@ -563,33 +601,46 @@ class ClockSampler:
 
     def window(self, t0, t1):
         """Clocks of the samples taken in [t0, t1] (wall time, seconds)."""
-        if self.proc is None:
-            return None
-        self.fh.flush()
         sm, mx, reasons = [], 0.0, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        a, b = datetime.datetime.fromtimestamp(t0), datetime.datetime.fromtimestamp(t1)
-        with open(self.path) as f:
-            for line in f:
-                parts = [p.strip() for p in line.split(",")]
-                if len(parts) < 9:
-                    continue
-                try:
-                    ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f")
-                    if ts < a or ts > b:
+        if self.thread is not None:
+            for t, s, m, rs in list(self.samples):
+                if t0 <= t <= t1:
+                    sm.append(s)
+                    mx = max(mx, m)
+                    reasons |= rs
+        elif self.proc is not None:
+            self.fh.flush()
+            a, b = datetime.datetime.fromtimestamp(t0), datetime.datetime.fromtimestamp(t1)
+            with open(self.path) as f:
+                for line in f:
+                    parts = [p.strip() for p in line.split(",")]
+                    if len(parts) < 9:
                         continue
-                    sm.append(float(parts[2]))
-                    mx = max(mx, float(parts[3]))
-                except ValueError:
-                    continue
-                for n, v in zip(names, parts[5:9]):
-                    if v.lower().startswith("active"):
-                        reasons.add(n)
+                    try:
+                        ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f")
+                        if ts < a or ts > b:
+                            continue
+                        sm.append(float(parts[2]))
+                        mx = max(mx, float(parts[3]))
+                    except ValueError:
+                        continue
+                    for n, v in zip(self.NAMES, parts[5:9]):
+                        if v.lower().startswith("active"):
+                            reasons.add(n)
         if not sm:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm),
+                "source": "nvml" if self.thread is not None else "nvidia-smi"}
 
     def stop(self):
+        if self.thread is not None:
+            self.halt.set()
+            self.thread.join(timeout=5)
+            try:
+                self.nv.nvmlShutdown()
+            except Exception:
+                pass
+            return
         if self.proc is None:
             return
         self.proc.terminate()
