@@ -107,11 +107,17 @@ def flash_attn_with_kvcache(
     scheduling hints (``num_splits``, ``pack_gqa``, ...) are not needed. The
     other flash-attn options raise ``NotImplementedError``.
     """
-    if _options_set(dict(qv=qv, rotary_cos=rotary_cos, rotary_sin=rotary_sin, cache_leftpad=cache_leftpad,
-                         cu_seqlens_q=cu_seqlens_q, cu_seqlens_k_new=cu_seqlens_k_new, max_seqlen_q=max_seqlen_q,
-                         rotary_seqlens=rotary_seqlens, q_descale=q_descale, k_descale=k_descale,
-                         v_descale=v_descale, window_size=window_size, softcap=softcap,
-                         attention_chunk=attention_chunk, alibi_slopes=alibi_slopes)):
+    # (every option at its default: the common case, decided without building
+    # the option table -- an engine calls this once per layer and token)
+    if not (qv is None and rotary_cos is None and rotary_sin is None and cache_leftpad is None
+            and cu_seqlens_q is None and cu_seqlens_k_new is None and max_seqlen_q is None
+            and rotary_seqlens is None and q_descale is None and k_descale is None and v_descale is None
+            and alibi_slopes is None and not attention_chunk and not softcap and window_size == (-1, -1)) \
+            and _options_set(dict(qv=qv, rotary_cos=rotary_cos, rotary_sin=rotary_sin, cache_leftpad=cache_leftpad,
+                                  cu_seqlens_q=cu_seqlens_q, cu_seqlens_k_new=cu_seqlens_k_new,
+                                  max_seqlen_q=max_seqlen_q, rotary_seqlens=rotary_seqlens, q_descale=q_descale,
+                                  k_descale=k_descale, v_descale=v_descale, window_size=window_size,
+                                  softcap=softcap, attention_chunk=attention_chunk, alibi_slopes=alibi_slopes)):
         raise NotImplementedError(_NOT_SUPPORTED)
     if block_table is not None and page_table is not None:
         raise ValueError("cpu_attention: pass `page_table` or `block_table`, not both")
