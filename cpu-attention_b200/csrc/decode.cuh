@@ -1037,9 +1037,9 @@ __global__ void __launch_bounds__(32 * (kDecodeMaxWarps + 2 + kDecodeFinishers),
   // registers (movmatrix), is P^T's B fragment; V's A fragments are 128-bit
   // row loads transposed the same way. P enters as bf16 plus its rounding
   // residual (two MMAs), so the weights keep ~16 bits like the fp32
-  // probabilities of the CUDA-core path. A page costs ~250 instructions
-  // instead of ~1600 at eight rows. MHA (GR = 1) and fp32 keep the CUDA-core
-  // path.
+  // probabilities of the CUDA-core path. A page's Q.K^T, softmax and P.V take
+  // ~250 instructions instead of ~1600 at eight rows. MHA (GR = 1) and fp32
+  // keep the CUDA-core path.
   constexpr bool kMMA = decode_uses_mma(Tile::kBF, GR);
   constexpr int NKS = E / 16;  // k-steps over the head dim
   constexpr int NT = E / 16;   // 16-dim tiles of O^T
