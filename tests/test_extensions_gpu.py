@@ -147,6 +147,21 @@ def test_gqa_engine_route_slots(dtype):
     assert torch.isfinite(lse).all()
 
 
+@pytest.mark.parametrize("page", [64, 128])
+@pytest.mark.parametrize("d", [64, 128])
+def test_gqa_decode_large_pages(page, d):
+    """Grouped bf16 rows on large pages: several 16-key blocks per page, the
+    online softmax carried across them and across the pages of a run, a
+    ragged last block over NaN-poisoned slots; against the C restatement."""
+    dtype, h, hk = torch.bfloat16, 16, 4
+    lens = [1, page - 1, page, page + 17, 3 * page + 5, 1000]
+    q, kc, vc, bt, ks, vs = stage_cache(lens, h, d, page, dtype, page + d, _store, device=DEV, gqa=hk)
+    L = torch.tensor(lens, dtype=torch.int32, device=DEV)
+    out = _api().flash_attn_with_kvcache(q, kc, vc, cache_seqlens=L, page_table=bt)
+    err, tol = north_star_ok(out[:, 0], _oracle_decode(q, kc, vc, bt, L, h), dtype)
+    assert err <= tol, err
+
+
 @pytest.mark.parametrize("dtype", cases.DTYPES)
 @pytest.mark.parametrize("h,hk", [(32, 8), (64, 8), (32, 1)])
 def test_gqa_decode_bitwise_reproducible(dtype, h, hk):
