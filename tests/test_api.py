@@ -36,6 +36,18 @@ def test_kvcache_unsupported_options(kwargs):
         C.flash_attn_with_kvcache(q, kc, vc, cache_seqlens=4, page_table=bt, **kwargs)
 
 
+@pytest.mark.parametrize("kwargs", [
+    dict(window_size=[-1, -1]), dict(softcap=0), dict(attention_chunk=0), dict(num_splits=4), dict(pack_gqa=True),
+    dict(scheduler_metadata=torch.ones(1)), dict(sm_margin=8), dict(causal=True), dict(rotary_interleaved=False),
+])
+def test_kvcache_inert_options_pass(kwargs):
+    """Options at an inert value, or scheduling hints, are accepted: the call
+    goes on to the device check (CPU tensors here)."""
+    q, kc, vc, bt = paged()
+    with pytest.raises(ValueError, match="CUDA"):
+        C.flash_attn_with_kvcache(q, kc, vc, cache_seqlens=4, page_table=bt, **kwargs)
+
+
 def test_kvcache_one_query_token_only():
     q, kc, vc, bt = paged()
     with pytest.raises(NotImplementedError):
