@@ -34,12 +34,19 @@ def balanced_ranges(lens, parts):
 def gather_outputs(out_local, counts, group=None):
     """The optional collective: every rank's decode output rows gathered in
     sequence order on every rank ([sum(counts), ...]). Uneven shards are padded
-    to the largest one for one all_gather_into_tensor, then unpadded."""
+    to the largest one for one all_gather_into_tensor, then unpadded; even ones
+    go straight into the result."""
     import torch
     import torch.distributed as dist
 
     world = dist.get_world_size(group)
     most = max(counts)
+    if min(counts) == most and out_local.is_contiguous():
+        # even shards: straight into the gathered tensor, nothing to pad or cut
+        full = torch.empty((world * most,) + tuple(out_local.shape[1:]), dtype=out_local.dtype,
+                           device=out_local.device)
+        dist.all_gather_into_tensor(full, out_local, group=group)
+        return full
     pad = torch.zeros((most,) + tuple(out_local.shape[1:]), dtype=out_local.dtype, device=out_local.device)
     pad[:out_local.shape[0]] = out_local
     full = torch.empty((world * most,) + tuple(out_local.shape[1:]), dtype=out_local.dtype,

@@ -77,3 +77,24 @@ def test_sharded_decode_gathers_to_the_unsharded_result(tmp_path):
     assert torch.equal(got["full"], ref)
     assert got["slowest"] == 2.0
     assert got["units"] == float(len(LENS))
+
+
+def _even_worker(rank, world, port, out_path):
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        local = torch.full((3, 2, 4), float(rank), dtype=torch.float32) + torch.arange(3.0)[:, None, None] / 10
+        full = gather_outputs(local, [3] * world)
+        if rank == 0:
+            torch.save(full, out_path)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_even_shards_gather_without_padding(tmp_path):
+    """Equal shard sizes take the direct all-gather (no pad, no cut); the
+    rows still come back in rank order."""
+    out_path = str(tmp_path / "even.pt")
+    mp.start_processes(_even_worker, args=(2, _free_port(), out_path), nprocs=2, join=True, start_method="spawn")
+    full = torch.load(out_path)
+    ref = torch.cat([torch.full((3, 2, 4), float(r)) + torch.arange(3.0)[:, None, None] / 10 for r in range(2)])
+    assert torch.equal(full, ref)
