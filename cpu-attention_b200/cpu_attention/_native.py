@@ -169,6 +169,13 @@ def store(rt, key, value, k_cache, v_cache, slots):
     to slot ``slots[i]`` (int64; negative skips it). True, or None
     (`_C.mojo:174-213`)."""
     del rt
+    fast = K.fastpath()
+    if fast is not None and _plain_tensors(key, value, k_cache, v_cache, slots):
+        # the same checks and call in C++ (cpu_attention/_fastpath)
+        done = fast.store(key, value, k_cache, v_cache, slots)
+        if done is not None and K.CHECK:
+            K.raise_status(key.device, K.current_stream(key.device))
+        return done
     dev = _cuda(key, value, k_cache, v_cache, slots)
     if dev is None or key.dim() != 3 or value.dim() != 3:
         return None

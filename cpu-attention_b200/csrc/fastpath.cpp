@@ -1,8 +1,8 @@
-// The decode and prefill entries' host path in C++: the same argument checks
-// as cpu_attention/_native.py::decode and ::flash (which mirror
-// `_C.mojo:87-171` and `:232-316`), done on at::Tensor fields instead of
-// Python attribute calls, then the C ABI call (ca_decode_ex / ca_flash_ex) on
-// the device's current stream. Varlen prefill and prefill log-sum-exp take the
+// The decode, prefill and store entries' host path in C++: the same argument
+// checks as cpu_attention/_native.py::decode, ::flash and ::store (which
+// mirror `_C.mojo:87-171`, `:232-316` and `:174-213`), done on at::Tensor
+// fields instead of Python attribute calls, then the C ABI call (ca_decode_ex /
+// ca_flash_ex / ca_store) on the device's current stream. Varlen prefill and prefill log-sum-exp take the
 // Python path. A decode step is short enough
 // (tens of µs) that the Python checks and the ctypes call were the larger part
 // of an end-to-end step's host time.
@@ -179,6 +179,39 @@ py::object flash(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, 
   return py::cast(out);
 }
 
+// reshape_and_cache: token i of key/value [tokens, heads, dim] to slot
+// slots[i] (int64; negative skips it): the checks of
+// cpu_attention/_native.py::store (`_C.mojo:174-213`), then ca_store. True, or
+// None when declined.
+py::object store(const at::Tensor& key, const at::Tensor& value, const at::Tensor& kc, const at::Tensor& vc,
+                 const at::Tensor& slots) {
+  if (!key.is_cuda()) return py::none();
+  const auto device = key.device();
+  auto same = [&](const at::Tensor& t) { return t.is_cuda() && t.device() == device; };
+  if (!same(value) || !same(kc) || !same(vc) || !same(slots)) return py::none();
+  if (key.dim() != 3 || value.dim() != 3) return py::none();
+  const int64_t n = key.size(0), heads = key.size(1), hd = key.size(2);
+  const int dt = dtype_code(key.scalar_type());
+  if (dt < 0 || !head_dim_ok(hd) || value.scalar_type() != key.scalar_type() || !rows_ok(key, hd)) return py::none();
+  if (value.sizes() != key.sizes() || value.strides() != key.strides()) return py::none();
+  if (kc.dim() != 4 || vc.sizes() != kc.sizes() || kc.scalar_type() != key.scalar_type() ||
+      vc.scalar_type() != key.scalar_type() || kc.size(1) != heads || kc.size(3) != hd || kc.size(2) <= 0 ||
+      kc.size(2) % 16 || !kc.is_contiguous() || !vc.is_contiguous())
+    return py::none();
+  if (!int_vector(slots, at::kLong, n)) return py::none();
+  if (n == 0) return py::bool_(true);
+  const int dev = device.index();
+  const c10::cuda::CUDAGuard guard(device);
+  cudaStream_t stream = c10::cuda::getCurrentCUDAStream(dev).stream();
+  at::Tensor ws = workspace(dev, (uintptr_t)stream, 0);
+  const int rc = ca_store(key.data_ptr(), value.data_ptr(), key.stride(0), kc.data_ptr(), vc.data_ptr(), kc.size(0),
+                          slots.data_ptr<int64_t>(), n, heads, hd, kc.size(2), dt,
+                          static_cast<int32_t*>(ws.data_ptr()), stream);
+  if (rc == CA_ECUDA) throw std::runtime_error(std::string("cpu_attention: ") + ca_last_cuda_error());
+  if (rc != CA_OK) return py::none();
+  return py::bool_(true);
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -188,6 +221,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("scale"), py::arg("dst"), py::arg("lse") = py::none());
   m.def("flash", &flash, "dense prefill; the output tensor, or None when declined", py::arg("q"), py::arg("k"),
         py::arg("v"), py::arg("scale"), py::arg("causal"));
+  m.def("store", &store, "reshape_and_cache; True, or None when declined", py::arg("key"), py::arg("value"),
+        py::arg("k_cache"), py::arg("v_cache"), py::arg("slots"));
   m.def("workspace", &py_workspace, "the workspace tensor of (device, stream), at least nbytes long",
         py::arg("device"), py::arg("stream"), py::arg("nbytes"));
 }

@@ -201,8 +201,8 @@ def test_library_exports_every_header_symbol():
 
 
 def test_decode_fast_path_is_built_and_declines_cpu_tensors():
-    """The C++ decode host path is built beside the kernel library, and it
-    declines (None) what the Python path declines -- here, CPU tensors -- so
+    """The C++ host path (decode, prefill, store) is built beside the kernel
+    library, and it declines (None) what the Python path declines -- here, CPU tensors -- so
     the reference's checks still raise the precise errors."""
     if os.environ.get("CPU_ATTENTION_SO"):
         pytest.skip("another kernel library is selected")
@@ -212,6 +212,8 @@ def test_decode_fast_path_is_built_and_declines_cpu_tensors():
     lens, pt = torch.zeros(2, dtype=torch.int32), torch.zeros(2, 2, dtype=torch.int32)
     assert fast.decode(q, q, q, None, None, None, lens, pt, None, None) is None
     assert fast.flash(q, q, q, None, True) is None
+    kv, cache = torch.zeros(3, 4, 64), torch.zeros(2, 4, 16, 64)
+    assert fast.store(kv, kv, cache, cache, torch.zeros(3, dtype=torch.int64)) is None
 
 
 def test_abi_declines_bad_arguments_without_a_device():
